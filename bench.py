@@ -1,0 +1,420 @@
+"""Benchmark: fused batchnorm + leaky forward and backward (BASELINE configs 0 and 1;
+config 4's sync-BN across GPUs when N > 1).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--shape B,C,H,W]
+
+A step is one training pass of one BN + leaky(0.1) layer over one batch:
+    forward  dnb_bn_act_forward_train  (read x, write y: 8 B/elem compulsory)
+    backward dnb_bn_act_backward       (read delta and x, write dx: 12 B/elem compulsory)
+on NCHW fp32 [128,128,32,32] per GPU (16.8 M elements, 64 MiB per tensor). With N > 1 GPUs
+every rank holds its own 128-image shard and the per-channel statistics are combined
+across ranks each step (sync-BN, global batch 128*N): weak scaling.
+
+Timing: W untimed steps, then K steps, each kernel preceded by an untimed write of a
+256 MiB buffer (larger than the 126 MB L2) so every timed kernel starts cold; CUDA events
+on the launching stream bracket each kernel; a barrier and a synchronize bracket the K
+steps; the reported time is the maximum over ranks. `value` is the algorithmic bytes of
+all ranks (20 B per element per step) divided by that time.
+
+`e2e` repeats the step through the C ABI with HOST buffers: x and delta are copied in
+from pinned memory and y and dx copied out every step, inside the timed region.
+
+`--impl reference` times the reference's CPU implementation of the same step (the C
+restatement of blas.zig / batchnorm.zig / activations.zig in oracle/, the reference's own
+Zig code having no toolchain here) on all host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+LEAKY = 7
+BYTES_FWD = 8   # per element: read x, write y
+BYTES_BWD = 12  # per element: read delta, read x, write dx
+HBM_NOMINAL_GBS = 8000.0  # BASELINE metric's "% of 8 TB/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--shape", default="128,128,32,32", help="per-GPU batch,channels,height,width")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    a = ap.parse_args()
+    a.warmup = max(a.warmup, 3)
+    a.shape = tuple(int(v) for v in a.shape.split(","))
+    return a
+
+
+def workload_desc(shape, n):
+    B, C, H, W = shape
+    return (f"BASELINE cfg0+cfg1: BN-train forward + leaky(0.1) then BN+leaky backward, NCHW fp32 "
+            f"[{B},{C},{H},{W}] per GPU" + (f"; sync-BN over {n} GPUs (global batch {B * n})" if n > 1 else ""))
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def profiled_traffic():
+    """dram bytes per launch of the backward kernel from the committed ncu summary."""
+    p = os.path.join(ROOT, "profiles", "bn_traffic.json")
+    if os.path.exists(p):
+        try:
+            return json.load(open(p))
+        except Exception:
+            return None
+    return None
+
+
+# ---- clocks ---------------------------------------------------------------------------
+
+class ClockSampler:
+    """nvidia-smi samples every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.lines = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.idx)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except FileNotFoundError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.thread.join(timeout=5)
+        sm, smax, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [v.strip() for v in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = max(smax, float(f[2]))
+            except ValueError:
+                continue
+            for name, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---- our implementation -----------------------------------------------------------------
+
+def run_ours(a):
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != a.gpus:
+        raise SystemExit(f"--gpus {a.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    from darknet_zig_b200 import gpu, syncbn
+
+    gpu.init(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as td
+
+        td.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+        dist = td
+    B, C, H, W = a.shape
+    S = H * W
+    E = B * C * S
+    dev = torch.device("cuda", local)
+    g = torch.Generator(device=dev)
+    g.manual_seed(1234 + rank)
+    x = torch.randn(E, generator=g, device=dev)
+    delta = torch.randn(E, generator=g, device=dev)
+    gamma = torch.rand(C, generator=g, device=dev) + 0.5
+    beta = torch.randn(C, generator=g, device=dev) * 0.1
+    y = torch.empty_like(x)
+    dx = torch.empty_like(x)
+    mean, var, rm, rv, bu, su, md, vd = (torch.zeros(C, device=dev) for _ in range(8))
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    layer = syncbn.SyncBN(B, C, S, world=world, dist=dist)
+
+    def fwd():
+        layer.forward(x, y, gamma, beta, mean, var, rm, rv, LEAKY)
+
+    def bwd():
+        layer.backward(x, delta, dx, gamma, beta, mean, var, bu, su, md, vd, LEAKY)
+
+    stream = torch.cuda.current_stream()
+    for _ in range(a.warmup):
+        flush.zero_()
+        fwd()
+        flush.zero_()
+        bwd()
+    torch.cuda.synchronize()
+    gpu.check_device_error()
+
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(a.steps)]
+    clocks = ClockSampler(local)
+    clocks.start()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    for k in range(a.steps):
+        flush.zero_()
+        ev[k][0].record(stream)
+        fwd()
+        ev[k][1].record(stream)
+        flush.zero_()
+        ev[k][2].record(stream)
+        bwd()
+        ev[k][3].record(stream)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    clk = clocks.stop()
+    gpu.check_device_error()
+    t_fwd = [e[0].elapsed_time(e[1]) for e in ev]
+    t_bwd = [e[2].elapsed_time(e[3]) for e in ev]
+    ms_fwd = sum(t_fwd) / a.steps
+    ms_bwd = sum(t_bwd) / a.steps
+    ms_step = ms_fwd + ms_bwd
+    if dist:
+        t = torch.tensor([ms_step, ms_fwd, ms_bwd], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_step, ms_fwd, ms_bwd = (float(v) for v in t.cpu())
+
+    e2e = None
+    if not a.no_e2e:
+        e2e = run_e2e(a, layer, x, y, delta, dx, gamma, beta, mean, var, rm, rv, bu, su, md, vd, dev, dist, world)
+
+    launches_per_step = layer.launches_per_step()
+    if dist:
+        # release NCCL state before the process group goes away
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    peak, peak_kind = measured_peaks()
+    bytes_step = (BYTES_FWD + BYTES_BWD) * E * world
+    value = bytes_step / (ms_step * 1e-3) / 1e9
+    bwd_gbs = BYTES_BWD * E / (ms_bwd * 1e-3) / 1e9
+    fwd_gbs = BYTES_FWD * E / (ms_fwd * 1e-3) / 1e9
+    traffic = profiled_traffic()
+    line = {
+        "metric": "fused BN+leaky forward+backward HBM throughput (algorithmic bytes / device time)",
+        "value": round(value, 2),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": a.steps,
+        "warmup": a.warmup,
+        "ms_per_step": round(ms_step, 5),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (torch.randn / rand, seeded per rank)",
+        "config": {"workload": workload_desc(a.shape, world), "batch_per_gpu": B, "channels": C, "hw": [H, W],
+                   "global_batch": B * world, "activation": "leaky 0.1",
+                   "l2": "256 MiB buffer written before every timed kernel (cold L2); 64 MiB tensors",
+                   "parallelism": f"dp{world}" + (" + sync-BN" if world > 1 else "")},
+        "elems_per_s": round(E * world / (ms_step * 1e-3), 1),
+        "pct_of_8TBs": round(100.0 * value / world / HBM_NOMINAL_GBS, 2),
+        "kernels": {
+            "bn_act_forward_train": {"ms": round(ms_fwd, 5), "GBps": round(fwd_gbs, 1),
+                                     "frac_of_peak": round(fwd_gbs / peak, 4), "bytes_per_elem": BYTES_FWD},
+            "bn_act_backward": {"ms": round(ms_bwd, 5), "GBps": round(bwd_gbs, 1),
+                                "frac_of_peak": round(bwd_gbs / peak, 4), "bytes_per_elem": BYTES_BWD},
+        },
+        "roofline": {"kernel": "bn_act_backward", "bound": "hbm", "achieved": round(bwd_gbs, 1), "peak": peak,
+                     "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                     else "fallback 6.65 TB/s", "unit": "GB/s", "frac": round(bwd_gbs / peak, 4),
+                     "traffic": (traffic or {}).get("bwd_dram_bytes_per_launch"),
+                     "algorithmic_bytes": BYTES_BWD * E},
+        "gpu_launches": launches_per_step * a.steps,
+        "clocks": clk,
+    }
+    if e2e:
+        line["e2e"] = e2e
+    if not a.no_cpu_baseline and world == 1:
+        line["cpu_baseline"] = cpu_baseline(a, threads=1)
+    print(json.dumps(line), flush=True)
+
+
+def run_e2e(a, layer, x, y, delta, dx, gamma, beta, mean, var, rm, rv, bu, su, md, vd, dev, dist, world):
+    """The step through the C ABI with host buffers: H2D of x and delta, fwd + bwd, D2H of
+    y and dx, all inside the timed region."""
+    import torch
+
+    E = x.numel()
+    hx = torch.empty(E, dtype=torch.float32, pin_memory=True)
+    hd = torch.empty(E, dtype=torch.float32, pin_memory=True)
+    hy = torch.empty(E, dtype=torch.float32, pin_memory=True)
+    hdx = torch.empty(E, dtype=torch.float32, pin_memory=True)
+    hx.copy_(x.cpu())
+    hd.copy_(delta.cpu())
+    stream = torch.cuda.current_stream()
+    steps = max(3, min(a.steps, 10))
+
+    def step():
+        x.copy_(hx, non_blocking=True)
+        delta.copy_(hd, non_blocking=True)
+        layer.forward(x, y, gamma, beta, mean, var, rm, rv, LEAKY)
+        layer.backward(x, delta, dx, gamma, beta, mean, var, bu, su, md, vd, LEAKY)
+        hy.copy_(y, non_blocking=True)
+        hdx.copy_(dx, non_blocking=True)
+
+    for _ in range(2):
+        step()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record(stream)
+    for _ in range(steps):
+        step()
+    e.record(stream)
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / steps
+    if dist:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = (BYTES_FWD + BYTES_BWD) * E * world / (ms * 1e-3) / 1e9
+    return {"value": round(value, 2), "unit": "GB/s", "ms_per_step": round(ms, 4), "steps": steps,
+            "h2d_bytes_per_step": 2 * E * 4, "d2h_bytes_per_step": 2 * E * 4,
+            "path": "C ABI with pinned host buffers; copies on the compute stream"}
+
+
+# ---- the reference's CPU implementation -----------------------------------------------------
+
+def cpu_step_sample(shape, threads, steps, warmup):
+    """Times the reference's op sequence (oracle restatement) for one BN+leaky training step."""
+    from darknet_zig_b200 import synth
+    from oracle.oracle import Oracle
+
+    orc = Oracle()
+    orc.set_threads(threads)
+    B, C, H, W = shape
+    S = H * W
+    E = B * C * S
+    x = synth.normal(1, (E,), 0, 1)
+    d0 = synth.normal(2, (E,), 0, 1)
+    gamma = synth.uniform(3, (C,), 0.5, 1.5)
+    beta = synth.normal(4, (C,), 0, 0.1)
+    y = np.zeros(E, np.float32)
+    xs = np.zeros(E, np.float32)
+    xn = np.zeros(E, np.float32)
+    z = lambda: np.zeros(C, np.float32)  # noqa: E731
+    mean, var, rm, rv, bu, su, md, vd = (z() for _ in range(8))
+    times = []
+    for i in range(warmup + steps):
+        delta = d0.copy()
+        t0 = time.perf_counter()
+        orc.bn_forward_layer(x, y, xs, xn, B, C, S, gamma, beta, mean, var, rm, rv, True, LEAKY)
+        orc.bn_backward_layer(xs, xn, y, delta, B, C, S, gamma, mean, var, bu, su, md, vd, LEAKY)
+        t1 = time.perf_counter()
+        if i >= warmup:
+            times.append(t1 - t0)
+    return sum(times) / len(times), E
+
+
+def cpu_baseline(a, threads):
+    # a bounded sample: as many full steps as fit ~10 s at this core count (at least 2)
+    t_one, E = cpu_step_sample(a.shape, threads, 1, 0)
+    steps = int(max(2, min(20, 10.0 / max(t_one, 1e-3))))
+    t, E = cpu_step_sample(a.shape, threads, steps, 1)
+    gbs = (BYTES_FWD + BYTES_BWD) * E / t / 1e9
+    return {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{steps} full steps of the workload (BN+leaky fwd+bwd, {E} elements) through the C "
+                      f"restatement of the reference CPU ops; {t * 1e3:.1f} ms/step; host {os.cpu_count()} cpus",
+            "ms_per_step": round(t * 1e3, 2), "elems_per_s": round(E / t, 1)}
+
+
+def run_reference(a):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    B, C, H, W = a.shape
+    t, E = cpu_step_sample(a.shape, threads, a.steps, a.warmup)
+    gbs = (BYTES_FWD + BYTES_BWD) * E / t / 1e9
+    line = {
+        "impl": "reference",
+        "metric": "fused BN+leaky forward+backward HBM throughput (algorithmic bytes / device time)",
+        "value": round(gbs, 3),
+        "unit": "GB/s",
+        "n_gpus": a.gpus,
+        "steps": a.steps,
+        "warmup": a.warmup,
+        "ms_per_step": round(t * 1e3, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded splitmix64 generator)",
+        "config": {"workload": workload_desc(a.shape, 1), "batch_per_gpu": B, "channels": C, "hw": [H, W],
+                   "parallelism": "host cores (reference CPU ops, OpenMP over channels)"},
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": f"{a.steps} full steps (after {a.warmup} warm-up) of the reference op sequence "
+                                   f"batchnorm.zig:74-123 + activations.zig, C restatement in oracle/"},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "elems_per_s": round(E / t, 1),
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    a = parse()
+    if a.impl == "reference":
+        run_reference(a)
+    else:
+        run_ours(a)
+
+
+if __name__ == "__main__":
+    main()

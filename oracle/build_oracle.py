@@ -1,0 +1,73 @@
+"""TEST INFRASTRUCTURE -- builds the CPU oracle and, where the reference tree is mounted,
+the reference's own kernel source as a host-emulated library.
+
+Outputs:
+  oracle/_build/liboracle.so   C restatement of the reference CPU ops (ref_ops.c)
+  oracle/_ref/libref_emulate.so  the reference's src/kernels/darknet_kernels.hip compiled
+                               by g++ for the host through hip_host_shim.h (built only
+                               when the reference tree is present; it then travels with
+                               the repository snapshot like any other built .so)
+
+Flags: -O3 -march=x86-64-v3 (AVX2+FMA, portable across the container and the GPU box
+hosts; -march=native could emit instructions another host lacks) and -ffp-contract=off,
+so no multiply-add is fused behind the restatement's back.
+"""
+from __future__ import annotations
+
+import os
+import subprocess
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+BUILD = os.path.join(HERE, "_build")
+REF_OUT = os.path.join(HERE, "_ref")
+ORACLE_SO = os.path.join(BUILD, "liboracle.so")
+REF_EMU_SO = os.path.join(REF_OUT, "libref_emulate.so")
+REFERENCE_KERNELS = os.environ.get(
+    "DNB_REFERENCE_KERNELS", "/root/reference/src/kernels/darknet_kernels.hip")
+
+CFLAGS = ["-O3", "-march=x86-64-v3", "-ffp-contract=off", "-fno-fast-math", "-fPIC", "-shared"]
+
+
+def _stale(out: str, deps: list[str]) -> bool:
+    if not os.path.exists(out):
+        return True
+    t = os.path.getmtime(out)
+    return any(os.path.getmtime(d) > t for d in deps if os.path.exists(d))
+
+
+def build_oracle(force: bool = False) -> str:
+    src = os.path.join(HERE, "ref_ops.c")
+    hdr = os.path.join(HERE, "ref_ops.h")
+    os.makedirs(BUILD, exist_ok=True)
+    if force or _stale(ORACLE_SO, [src, hdr, __file__]):
+        cmd = ["gcc", *CFLAGS, "-fopenmp", "-Wall", "-o", ORACLE_SO, src, "-lm"]
+        subprocess.check_call(cmd)
+    return ORACLE_SO
+
+
+def build_ref_emulation(force: bool = False) -> str | None:
+    """Compile the reference's own kernel file for the host. Returns None when the
+    reference tree is not mounted (e.g. on the GPU box, which uses the prebuilt file)."""
+    if not os.path.exists(REFERENCE_KERNELS):
+        return REF_EMU_SO if os.path.exists(REF_EMU_SO) else None
+    src = os.path.join(HERE, "ref_emulate.cpp")
+    shim = os.path.join(HERE, "hip_host_shim.h")
+    os.makedirs(REF_OUT, exist_ok=True)
+    if force or _stale(REF_EMU_SO, [src, shim, REFERENCE_KERNELS, __file__]):
+        cmd = ["g++", "-std=c++20", *CFLAGS, "-w", "-pthread", "-I", os.path.join(HERE, "shim"),
+               f"-DDNB_REFERENCE_KERNELS=\"{REFERENCE_KERNELS}\"",
+               "-o", REF_EMU_SO, src, "-lm"]
+        subprocess.check_call(cmd)
+    return REF_EMU_SO
+
+
+def build_all(force: bool = False) -> None:
+    build_oracle(force)
+    build_ref_emulation(force)
+
+
+if __name__ == "__main__":
+    build_all(force="--force" in sys.argv)
+    print(ORACLE_SO)
+    print(REF_EMU_SO if os.path.exists(REF_EMU_SO) else "(reference emulation not built)")

@@ -1,0 +1,59 @@
+"""Shared fixtures. Tests marked `gpu` need a CUDA device and the built libdnb200.so; they
+fail (never skip) when either is missing, so a GPU run that silently falls back cannot
+pass. Everything else runs on the CPU."""
+from __future__ import annotations
+
+import os
+import sys
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA device (B200) and the built libdnb200.so")
+    config.addinivalue_line("markers", "slow: full BASELINE-size case")
+
+
+@pytest.fixture(scope="session")
+def oracle():
+    from oracle.oracle import get_oracle
+
+    return get_oracle()
+
+
+@pytest.fixture(scope="session")
+def ref_emulation():
+    from oracle.oracle import RefEmulation
+
+    try:
+        return RefEmulation()
+    except FileNotFoundError as e:
+        pytest.skip(str(e))
+
+
+@pytest.fixture(scope="session")
+def built_lib():
+    """Path of libdnb200.so, (re)building it first when a source is newer (nvcc
+    cross-compiles, so this works without a GPU). On a box without nvcc the prebuilt
+    library is used as is."""
+    from darknet_zig_b200 import build
+
+    if os.path.exists(build.NVCC):
+        build.build()
+    assert os.path.exists(build.LIB), "libdnb200.so is missing and cannot be built here"
+    return build.LIB
+
+
+@pytest.fixture(scope="session")
+def cuda(built_lib):
+    import torch
+
+    assert torch.cuda.is_available(), "GPU test run without a CUDA device"
+    from darknet_zig_b200 import gpu
+
+    gpu.init(0)
+    return torch.device("cuda", 0)
