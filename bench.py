@@ -89,60 +89,83 @@ def profiled_traffic():
 # ---- clocks ---------------------------------------------------------------------------
 
 class ClockSampler:
-    """nvidia-smi samples every 200 ms during the timed region."""
+    """SM clock and clock-event reasons sampled every ~2 ms through NVML (read-only queries)
+    from a background thread while the timed region runs; nvidia-smi once as a fallback."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"),
+               ("hw_power_brake_slowdown", "nvmlClocksEventReasonHwPowerBrakeSlowdown"))
 
     def __init__(self, gpu_index: int):
         self.idx = gpu_index
-        self.proc = None
-        self.lines = []
+        self.samples = []
+        self.stop_evt = threading.Event()
         self.thread = None
+        self.nvml = None
+        self.handle = None
 
     def start(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
-                 "-i", str(self.idx)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except FileNotFoundError:
-            self.proc = None
+            import pynvml
+
+            pynvml.nvmlInit()
+            uuid = None
+            try:
+                import torch
+
+                uuid = "GPU-" + str(torch.cuda.get_device_properties(self.idx).uuid)
+            except Exception:
+                pass
+            self.handle = (pynvml.nvmlDeviceGetHandleByUUID(uuid) if uuid else
+                           pynvml.nvmlDeviceGetHandleByIndex(self.idx))
+            self.nvml = pynvml
+        except Exception:
+            self.nvml = None
             return
-        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread = threading.Thread(target=self._poll, daemon=True)
         self.thread.start()
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+    def _poll(self):
+        n = self.nvml
+        while not self.stop_evt.is_set():
+            try:
+                sm = n.nvmlDeviceGetClockInfo(self.handle, n.NVML_CLOCK_SM)
+                bits = n.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+                self.samples.append((sm, bits))
+            except Exception:
+                break
+            time.sleep(0.002)
 
     def stop(self):
-        if self.proc is None:
-            return None
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
+        if self.nvml is None:
+            return self._smi_once()
+        self.stop_evt.set()
         self.thread.join(timeout=5)
-        sm, smax, reasons = [], 0.0, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            f = [v.strip() for v in ln.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1]))
-                smax = max(smax, float(f[2]))
-            except ValueError:
-                continue
-            for name, v in zip(names, f[5:9]):
-                if v.lower() == "active":
-                    reasons.add(name)
-        if not sm:
+        n = self.nvml
+        try:
+            smax = float(n.nvmlDeviceGetMaxClockInfo(self.handle, n.NVML_CLOCK_SM))
+        except Exception:
+            smax = None
+        if not self.samples:
             return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        reasons = set()
+        for _, bits in self.samples:
+            for name, const in self.REASONS:
+                if bits & getattr(n, const, 0):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(s for s, _ in self.samples), "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(self.samples), "source": "nvml"}
+
+    def _smi_once(self):
+        try:
+            out = subprocess.run(["nvidia-smi", "--query-gpu=clocks.sm,clocks.max.sm", "--format=csv,noheader,nounits",
+                                  "-i", str(self.idx)], capture_output=True, text=True, timeout=10).stdout
+            sm, smax = (float(v) for v in out.strip().split(","))
+            return {"sm_mhz": sm, "sm_max_mhz": smax, "reasons": [], "samples": 1, "source": "nvidia-smi after"}
+        except Exception:
+            return None
 
 
 # ---- our implementation -----------------------------------------------------------------

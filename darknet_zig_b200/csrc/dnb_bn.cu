@@ -31,6 +31,8 @@
 // Per-element arithmetic follows the reference CPU code (blas.zig:137-204) operation by
 // operation without fused roundings (--fmad=false), so given the same per-channel
 // statistics the outputs are bit-identical to it.
+#include <math.h>
+
 #include <cooperative_groups.h>
 
 #include "dnb_chan.cuh"
@@ -431,7 +433,8 @@ dnb_status generic_bwd_apply(const GGeom &g, const float *x, const float *y, con
 // persistent fused kernel
 // ======================================================================================
 
-constexpr int kPThreads = 512;
+constexpr int kPThreads = 256;
+constexpr int kPMinBlocks = 2;  // CTAs per SM the register budget is sized for
 constexpr int kMaxStages = 3;
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -462,15 +465,20 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, unsigned by
                  : "memory");
 }
 
-// Everything the persistent kernel needs, by value.
+// Everything the persistent kernel needs, by value. All partition arithmetic is 32-bit
+// with FastDiv: the plan guarantees cap_units * P * P < 2^32, which bounds every product
+// below (p*T, (t+1)*P with T <= cap_units*P).
 struct PArgs {
     // geometry
     int64_t C, S;
     int N, K, U, NK;       // batch, units per plane, unit floats, units per channel
     int cg, G, P;          // channels per group, groups, CTAs
     int cap_units, maxj, stages;
-    FastDiv f_u4, f_nk, f_k;
+    uint32_t T_full, T_last;  // units in a group (every group but the last / the last)
+    FastDiv f_u4, f_nk, f_k, f_p, f_tfull, f_tlast;
     float denom;           // batch*spatial as f32 (normalize_delta's denominator)
+    float inv_denom;       // 1/denom, used only when denom is a power of two (then exact)
+    int denom_pow2;
     // tensors: fwd uses t0 = x; bwd uses t0 = delta, t1 = x, t2 = y (optional)
     const float *t0, *t1, *t2;
     float *out, *xnorm;
@@ -493,25 +501,34 @@ struct UnitEntry {
     int pad;
 };
 
-// Shares of group g: units [t0, t1) of T = cg_g * NK, channel base c0.
+// Share of CTA p in group g: units [t0, t1) of the group's T (channel base c0).
 struct Share {
-    int64_t c0, T, t0, t1;
+    uint32_t c0, T, t0, t1;
     int cfirst, clast;  // local channel indices touched (inclusive); cfirst > clast when empty
 };
 __device__ __forceinline__ Share share_of(const PArgs &a, int g, int p) {
     Share s;
-    s.c0 = (int64_t)g * a.cg;
-    int64_t cgg = a.C - s.c0;
-    if (cgg > a.cg) cgg = a.cg;
-    s.T = cgg * a.NK;
-    s.t0 = (int64_t)p * s.T / a.P;
-    s.t1 = (int64_t)(p + 1) * s.T / a.P;
-    s.cfirst = (int)(s.t0 / a.NK);
-    s.clast = s.t1 > s.t0 ? (int)((s.t1 - 1) / a.NK) : s.cfirst - 1;
+    s.c0 = (uint32_t)g * (uint32_t)a.cg;
+    s.T = g == a.G - 1 ? a.T_last : a.T_full;
+    s.t0 = a.f_p.div((uint32_t)p * s.T);
+    s.t1 = a.f_p.div((uint32_t)(p + 1) * s.T);
+    s.cfirst = (int)a.f_nk.div(s.t0);
+    s.clast = s.t1 > s.t0 ? (int)a.f_nk.div(s.t1 - 1) : s.cfirst - 1;
     return s;
 }
-// The CTA that owns unit t of a group with T units.
-__device__ __forceinline__ int owner_of(int64_t t, int64_t T, int P) { return (int)(((t + 1) * P - 1) / T); }
+// The CTA that owns unit t of group g: the largest p with floor(p*T/P) <= t.
+__device__ __forceinline__ int owner_of(const PArgs &a, int g, uint32_t t) {
+    const FastDiv &fd = g == a.G - 1 ? a.f_tlast : a.f_tfull;
+    return (int)fd.div((t + 1) * (uint32_t)a.P - 1);
+}
+
+__device__ __forceinline__ float div_denom(float v, const PArgs &a) {
+    return a.denom_pow2 ? v * a.inv_denom : v / a.denom;
+}
+// dx as bn_dx1, with the division by a power-of-two denominator done as an exact multiply
+__device__ __forceinline__ float bn_dx_p(float gval, float x, const BwdParam &p, const PArgs &a) {
+    return (gval * p.g) * p.inv2 + div_denom(p.vd * 2.0f * (x - p.m), a) + p.mdd;
+}
 
 template <bool BWD, int A, bool HASY>
 struct PKernel {
@@ -573,11 +590,11 @@ struct PKernel {
         __syncwarp();
         const float *src[3] = {a.t0, a.t1, a.t2};
         for (int u = threadIdx.x; u < n_units; u += 32) {
-            const int64_t t = sh.t0 + u;
+            const uint32_t t = sh.t0 + u;
             uint32_t cl, rem, n, k;
-            a.f_nk.divmod((uint32_t)t, cl, rem);
+            a.f_nk.divmod(t, cl, rem);
             a.f_k.divmod(rem, n, k);
-            const int64_t c = sh.c0 + cl;
+            const int64_t c = (int64_t)sh.c0 + cl;
             const int64_t goff = ((int64_t)n * a.C + c) * a.S + (int64_t)k * a.U;
             s.units[stage * a.cap_units + u] = UnitEntry{goff, (int)cl - sh.cfirst, 0};
 #pragma unroll
@@ -601,27 +618,28 @@ struct PKernel {
     }
 
     // Per-channel partial of one share segment (the whole block; result valid in thread 0).
-    __device__ static float2 segment_stats(const PArgs &a, const Smem &s, int stage, int64_t ua, int64_t ub,
-                                           int64_t c) {
-        const int64_t f0 = ua * a.U, f1 = ub * a.U;  // float range in the stage buffer
+    __device__ static float2 segment_stats(const PArgs &a, const Smem &s, int stage, int ua, int ub, int64_t c) {
+        const int q0 = ua * (a.U >> 2), q1 = ub * (a.U >> 2);  // float4 range in the stage buffer
         const float4 *b0 = reinterpret_cast<const float4 *>(tensor_buf(a, s, stage, 0));
-        const int64_t q0 = f0 >> 2, q1 = f1 >> 2;
         if constexpr (!BWD) {
-            // two-pass mean / M2 from shared memory
-            float acc = 0.0f;
-            for (int64_t q = q0 + threadIdx.x; q < q1; q += kPThreads) {
+            // one pass: per-thread sums shifted by the thread's first element, then the block
+            // merges (count, mean, M2) of its threads (Chan et al.)
+            float shift = 0.0f, s1 = 0.0f, s2 = 0.0f, nt = 0.0f;
+            if (q0 + (int)threadIdx.x < q1) shift = b0[q0 + threadIdx.x].x;
+            for (int q = q0 + threadIdx.x; q < q1; q += kPThreads) {
                 const float4 v = b0[q];
-                acc += (v.x + v.y) + (v.z + v.w);
+                const float d0 = v.x - shift, d1 = v.y - shift, d2 = v.z - shift, d3 = v.w - shift;
+                s1 += (d0 + d1) + (d2 + d3);
+                s2 += (d0 * d0 + d1 * d1) + (d2 * d2 + d3 * d3);
+                nt += 4.0f;
             }
-            const float cnt = (float)(f1 - f0);
-            const float mr = block_sum<kPThreads>(acc, s.red) / cnt;
-            float acc2 = 0.0f;
-            for (int64_t q = q0 + threadIdx.x; q < q1; q += kPThreads) {
-                const float4 v = b0[q];
-                const float d0 = v.x - mr, d1 = v.y - mr, d2 = v.z - mr, d3 = v.w - mr;
-                acc2 += (d0 * d0 + d1 * d1) + (d2 * d2 + d3 * d3);
-            }
-            const float m2 = block_sum<kPThreads>(acc2, s.red);
+            const float cnt = (float)((q1 - q0) * 4);
+            const float mt = nt > 0.0f ? shift + s1 / nt : 0.0f;
+            float m2t = nt > 0.0f ? s2 - s1 * (s1 / nt) : 0.0f;
+            if (m2t < 0.0f) m2t = 0.0f;
+            const float mr = block_sum<kPThreads>(nt > 0.0f ? nt * shift + s1 : 0.0f, s.red) / cnt;
+            const float dm = mt - mr;
+            const float m2 = block_sum<kPThreads>(nt > 0.0f ? m2t + nt * dm * dm : 0.0f, s.red);
             return make_float2(mr, m2);
         } else {
             const float4 *bx = reinterpret_cast<const float4 *>(tensor_buf(a, s, stage, 1));
@@ -632,7 +650,7 @@ struct PKernel {
             p.g = a.scales[c];
             p.b = a.biases[c];
             float s1 = 0.0f, s2 = 0.0f;
-            for (int64_t q = q0 + threadIdx.x; q < q1; q += kPThreads) {
+            for (int q = q0 + threadIdx.x; q < q1; q += kPThreads) {
                 const float4 d = b0[q], xv = bx[q];
                 const float4 yv = HASY ? by[q] : xv;
                 const float g0 = bn_grad1<A, HASY>(d.x, xv.x, yv.x, p, a.act);
@@ -650,25 +668,29 @@ struct PKernel {
     __device__ static void stats(const PArgs &a, const Smem &s, int g, int stage) {
         const Share sh = share_of(a, g, blockIdx.x);
         for (int cl = sh.cfirst; cl <= sh.clast; ++cl) {
-            int64_t ua = (int64_t)cl * a.NK, ub = ua + a.NK;
+            uint32_t ua = (uint32_t)cl * a.NK, ub = ua + a.NK;
             if (ua < sh.t0) ua = sh.t0;
             if (ub > sh.t1) ub = sh.t1;
-            const float2 r = segment_stats(a, s, stage, ua - sh.t0, ub - sh.t0, sh.c0 + cl);
+            const float2 r = segment_stats(a, s, stage, (int)(ua - sh.t0), (int)(ub - sh.t0), (int64_t)sh.c0 + cl);
             if (threadIdx.x == 0)
                 a.rec[((int64_t)g * a.P + blockIdx.x) * a.maxj + (cl - sh.cfirst)] = r;
         }
     }
 
-    __device__ static bool arrive_and_wait(const PArgs &a, const Smem &s, unsigned *cnt, int g, bool last_group,
-                                           unsigned epoch) {
-        __syncthreads();
+    // Publish this CTA's records of group g: fence, then one arrival on the group counter.
+    __device__ static void arrive(const PArgs &a, unsigned *cnt, int g, bool last_group, unsigned epoch) {
         if (threadIdx.x == 0) {
             __threadfence();
             const unsigned prev = atomicAdd(&cnt[g], 1u);
-            if (last_group && prev == (unsigned)a.P - 1) {
-                // every CTA has read the epoch (it arrived here after doing so): advance it
-                atomicExch(&a.sync[0], epoch + 1);
-            }
+            // every CTA read the epoch before its first arrival: the last one of the last
+            // group advances it for the next launch
+            if (last_group && prev == (unsigned)a.P - 1) atomicExch(&a.sync[0], epoch + 1);
+        }
+    }
+
+    // Wait (bounded) until every CTA has arrived on group g; block-uniform result.
+    __device__ static bool wait_group(const PArgs &a, const Smem &s, unsigned *cnt, int g) {
+        if (threadIdx.x == 0) {
             int ok = 1;
             const unsigned long long deadline = global_ns() + a.wait_ns;
             while (ld_acquire_gpu(&cnt[g]) < (unsigned)a.P) {
@@ -682,7 +704,7 @@ struct PKernel {
                     ok = 0;
                     break;
                 }
-                __nanosleep(40);
+                __nanosleep(32);
             }
             *s.flag = ok;
         }
@@ -696,32 +718,44 @@ struct PKernel {
         const Share sh = share_of(a, g, blockIdx.x);
         const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
         for (int cl = sh.cfirst + warp; cl <= sh.clast; cl += kPThreads / 32) {
-            const int64_t c = sh.c0 + cl;
-            const int64_t ua = (int64_t)cl * a.NK, ub = ua + a.NK;
-            const int plo = owner_of(ua, sh.T, a.P), phi = owner_of(ub - 1, sh.T, a.P);
+            const int64_t c = (int64_t)sh.c0 + cl;
+            const uint32_t ua = (uint32_t)cl * a.NK, ub = ua + a.NK;
+            const int plo = owner_of(a, g, ua), phi = owner_of(a, g, ub - 1);
             const bool write = plo == (int)blockIdx.x;
             float *out = s.ptab + (cl - sh.cfirst) * 8;
+            // CTAs between plo and phi with no unit of this channel (a group with fewer
+            // units than CTAs) wrote no record for it: skip them
             if constexpr (!BWD) {
-                // CTAs between plo and phi with no unit of this channel (a group with fewer
-                // units than CTAs) wrote no record for it: skip them
-                double cm = 0.0;
+                double cm = 0.0, n_r = 0.0, m_r = 0.0, q_r = 0.0;
+                bool have = false;
                 for (int p = plo + lane; p <= phi; p += 32) {
                     const Share o = share_of(a, g, p);
-                    const int64_t lo = ua > o.t0 ? ua : o.t0, hi = ub < o.t1 ? ub : o.t1;
+                    const uint32_t lo = ua > o.t0 ? ua : o.t0, hi = ub < o.t1 ? ub : o.t1;
                     if (hi <= lo) continue;
                     const float2 r = __ldcg(&a.rec[((int64_t)g * a.P + p) * a.maxj + (cl - o.cfirst)]);
-                    cm += (double)((hi - lo) * a.U) * (double)r.x;
+                    const double nr = (double)((hi - lo) * (uint32_t)a.U);
+                    cm += nr * (double)r.x;
+                    if (p + 32 > phi) {  // the common case: one record per lane
+                        n_r = nr;
+                        m_r = r.x;
+                        q_r = r.y;
+                        have = true;
+                    }
                 }
                 const double n = (double)a.NK * a.U;
                 const double mu = warp_sum(cm) / n;
                 double m2 = 0.0;
-                for (int p = plo + lane; p <= phi; p += 32) {
-                    const Share o = share_of(a, g, p);
-                    const int64_t lo = ua > o.t0 ? ua : o.t0, hi = ub < o.t1 ? ub : o.t1;
-                    if (hi <= lo) continue;
-                    const float2 r = __ldcg(&a.rec[((int64_t)g * a.P + p) * a.maxj + (cl - o.cfirst)]);
-                    const double d = (double)r.x - mu;
-                    m2 += (double)r.y + (double)((hi - lo) * a.U) * d * d;
+                if (phi - plo < 32) {
+                    if (have) m2 = q_r + n_r * (m_r - mu) * (m_r - mu);
+                } else {
+                    for (int p = plo + lane; p <= phi; p += 32) {
+                        const Share o = share_of(a, g, p);
+                        const uint32_t lo = ua > o.t0 ? ua : o.t0, hi = ub < o.t1 ? ub : o.t1;
+                        if (hi <= lo) continue;
+                        const float2 r = __ldcg(&a.rec[((int64_t)g * a.P + p) * a.maxj + (cl - o.cfirst)]);
+                        const double d = (double)r.x - mu;
+                        m2 += (double)r.y + (double)((hi - lo) * (uint32_t)a.U) * d * d;
+                    }
                 }
                 m2 = warp_sum(m2);
                 if (lane == 0) {
@@ -741,7 +775,7 @@ struct PKernel {
                 double s1 = 0.0, s2 = 0.0;
                 for (int p = plo + lane; p <= phi; p += 32) {
                     const Share o = share_of(a, g, p);
-                    const int64_t lo = ua > o.t0 ? ua : o.t0, hi = ub < o.t1 ? ub : o.t1;
+                    const uint32_t lo = ua > o.t0 ? ua : o.t0, hi = ub < o.t1 ? ub : o.t1;
                     if (hi <= lo) continue;
                     const float2 r = __ldcg(&a.rec[((int64_t)g * a.P + p) * a.maxj + (cl - o.cfirst)]);
                     s1 += (double)r.x;
@@ -763,7 +797,7 @@ struct PKernel {
     __device__ static void apply(const PArgs &a, const Smem &s, int g, int stage) {
         const Share sh = share_of(a, g, blockIdx.x);
         const uint32_t u4 = (uint32_t)a.U >> 2;
-        const uint32_t n4 = (uint32_t)(sh.t1 - sh.t0) * u4;
+        const uint32_t n4 = (sh.t1 - sh.t0) * u4;
         const float4 *b0 = reinterpret_cast<const float4 *>(tensor_buf(a, s, stage, 0));
         const UnitEntry *ut = s.units + stage * a.cap_units;
         if constexpr (!BWD) {
@@ -793,18 +827,40 @@ struct PKernel {
                 const float4 d = b0[i], xv = bx[i];
                 const float4 yv = HASY ? by[i] : xv;
                 const int64_t off = e.goff + 4 * (int64_t)r;
-                st4(a.out + off,
-                    make_float4(bn_dx1(bn_grad1<A, HASY>(d.x, xv.x, yv.x, p, a.act), xv.x, p, a.denom),
-                                bn_dx1(bn_grad1<A, HASY>(d.y, xv.y, yv.y, p, a.act), xv.y, p, a.denom),
-                                bn_dx1(bn_grad1<A, HASY>(d.z, xv.z, yv.z, p, a.act), xv.z, p, a.denom),
-                                bn_dx1(bn_grad1<A, HASY>(d.w, xv.w, yv.w, p, a.act), xv.w, p, a.denom)));
+                st4(a.out + off, make_float4(bn_dx_p(bn_grad1<A, HASY>(d.x, xv.x, yv.x, p, a.act), xv.x, p, a),
+                                             bn_dx_p(bn_grad1<A, HASY>(d.y, xv.y, yv.y, p, a.act), xv.y, p, a),
+                                             bn_dx_p(bn_grad1<A, HASY>(d.z, xv.z, yv.z, p, a.act), xv.z, p, a),
+                                             bn_dx_p(bn_grad1<A, HASY>(d.w, xv.w, yv.w, p, a.act), xv.w, p, a)));
             }
         }
     }
 };
 
+#ifdef DNB_PHASE_TIMING
+// Diagnostic build only (-DDNB_PHASE_TIMING): %globaltimer stamps per (CTA, group, phase):
+// 0 copies landed, 1 partials published, 2 group barrier released, 3 merge done, 4 apply done.
+constexpr int kTsCtas = 160, kTsGroups = 64, kTsPhases = 6;
+__device__ unsigned long long g_phase_ts[kTsCtas * kTsGroups * kTsPhases];
+#define DNB_STAMP(g, ph)                                                                              \
+    do {                                                                                              \
+        if (threadIdx.x == 0 && blockIdx.x < kTsCtas && (g) < kTsGroups)                              \
+            g_phase_ts[(blockIdx.x * kTsGroups + (g)) * kTsPhases + (ph)] = global_ns();              \
+    } while (0)
+#else
+#define DNB_STAMP(g, ph) \
+    do {                 \
+    } while (0)
+#endif
+
+// Software pipeline, `stages` groups deep. Iteration g:
+//   wait for group g+1's copies; reduce them; publish (arrive on g+1)
+//   wait for group g's arrivals (published one iteration earlier, so normally complete)
+//   merge group g's records; write group g's outputs from shared memory
+//   refill the freed stage with group g+stages
+// The copy of a group is issued `stages - 1` iterations before it is reduced, and the
+// grid-wide wait for a group trails its arrivals by one iteration of work.
 template <bool BWD, int A, bool HASY>
-__global__ void __launch_bounds__(kPThreads, 1) k_bn_persistent(PArgs a) {
+__global__ void __launch_bounds__(kPThreads, kPMinBlocks) k_bn_persistent(PArgs a) {
     using K = PKernel<BWD, A, HASY>;
     extern __shared__ __align__(128) unsigned char smem_raw[];
     const typename K::Smem s = K::carve(a, smem_raw);
@@ -826,7 +882,6 @@ __global__ void __launch_bounds__(kPThreads, 1) k_bn_persistent(PArgs a) {
     // pending[st] = parity of the copy outstanding on stage st, or -1
     int pending[kMaxStages] = {-1, -1, -1};
     unsigned uses[kMaxStages] = {0, 0, 0};
-    bool ok = true;
 
     const int pre = a.G < a.stages ? a.G : a.stages;
     for (int g = 0; g < pre; ++g) {
@@ -834,30 +889,39 @@ __global__ void __launch_bounds__(kPThreads, 1) k_bn_persistent(PArgs a) {
         pending[g] = (int)(uses[g] & 1u);
         ++uses[g];
     }
-    // stats of group 0
-    ok = K::wait_copies(a, s, 0, (unsigned)pending[0]);
+    // every wait result is made block-uniform before it steers control flow, so no thread
+    // can leave the loop while others continue into a barrier
+    bool ok = __syncthreads_and(K::wait_copies(a, s, 0, (unsigned)pending[0])) != 0;
+    DNB_STAMP(0, 0);
     if (ok) {
         K::stats(a, s, 0, 0);
-        ok = K::arrive_and_wait(a, s, cnt, 0, a.G == 1, epoch);
+        K::arrive(a, cnt, 0, a.G == 1, epoch);
+        DNB_STAMP(0, 1);
     }
     for (int g = 0; ok && g < a.G; ++g) {
         const int st = g % a.stages;
-        // group g's arrivals are complete here (the wait follows stats(g))
+        if (g + 1 < a.G) {
+            const int st1 = (g + 1) % a.stages;
+            ok = __syncthreads_and(K::wait_copies(a, s, st1, (unsigned)pending[st1])) != 0;
+            DNB_STAMP(g + 1, 0);
+            if (!ok) break;
+            K::stats(a, s, g + 1, st1);
+            K::arrive(a, cnt, g + 1, g + 2 == a.G, epoch);
+            DNB_STAMP(g + 1, 1);
+        }
+        ok = K::wait_group(a, s, cnt, g);
+        DNB_STAMP(g, 2);
+        if (!ok) break;
         K::finalize(a, s, g);
+        DNB_STAMP(g, 3);
         K::apply(a, s, g, st);
         pending[st] = -1;
         __syncthreads();  // every thread is done reading stage st
+        DNB_STAMP(g, 4);
         if (g + a.stages < a.G) {
             K::issue(a, s, g + a.stages, st);
             pending[st] = (int)(uses[st] & 1u);
             ++uses[st];
-        }
-        if (g + 1 < a.G) {
-            const int st1 = (g + 1) % a.stages;
-            ok = K::wait_copies(a, s, st1, (unsigned)pending[st1]);
-            if (!ok) break;
-            K::stats(a, s, g + 1, st1);
-            ok = K::arrive_and_wait(a, s, cnt, g + 1, g + 2 == a.G, epoch);
         }
     }
     if (!ok) {
@@ -869,7 +933,7 @@ __global__ void __launch_bounds__(kPThreads, 1) k_bn_persistent(PArgs a) {
 
 struct PPlan {
     bool ok = false;
-    int K, U, cap_units, cg, G, P, maxj, stages;
+    int K, U, cap_units, cg, G, P, maxj, stages, ctas_per_sm;
     size_t smem;
 };
 
@@ -881,7 +945,15 @@ PPlan plan_persistent(int64_t batch, int64_t filters, int64_t spatial, const Dev
     PPlan pl;
     if (spatial % 4 != 0 || batch <= 0 || filters <= 0) return pl;
     const int nt = K::NT;
-    const size_t budget = (size_t)ds->max_smem_optin - 8192;  // unit tables, records, barriers
+    // CTAs per SM: two by default, so one CTA's barrier wait and merge overlap the other's
+    // reduction and writes
+    const char *env_c = getenv("DNB_BN_CTAS_PER_SM");
+    int ctas = env_c ? atoi(env_c) : 2;
+    if (ctas < 1) ctas = 1;
+    if (ctas > 4) ctas = 4;
+    size_t per_cta = (size_t)ds->smem_per_sm / ctas - (size_t)ds->smem_reserved - 256;  // 256: static smem
+    if (per_cta > (size_t)ds->max_smem_optin) per_cta = (size_t)ds->max_smem_optin;
+    const size_t budget = per_cta - 4096;  // unit tables, apply records, reduction scratch, barriers
     const size_t per_tensor = budget / ((size_t)stages * nt);
     // smallest K dividing spatial with U % 4 == 0 and one unit fitting a stage buffer
     int64_t k = 1;
@@ -893,7 +965,7 @@ PPlan plan_persistent(int64_t batch, int64_t filters, int64_t spatial, const Dev
     if (k > spatial) return pl;
     const int64_t U = spatial / k, NK = batch * k;
     int64_t cap = (int64_t)(per_tensor / ((size_t)U * 4));
-    const int64_t P = ds->sm_count;
+    const int64_t P = (int64_t)ds->sm_count * ctas;
     int64_t cg_max = cap * P / NK;
     if (cg_max < 1) return pl;
     // at least ~6 groups so the copy of the next group overlaps the current one
@@ -910,7 +982,8 @@ PPlan plan_persistent(int64_t batch, int64_t filters, int64_t spatial, const Dev
     if (G > kMaxGroups) return pl;
     const int64_t share = (cg * NK + P - 1) / P;
     if (share > cap) return pl;
-    if ((int64_t)P * cg * NK >= (1ll << 31)) return pl;  // 32-bit unit arithmetic
+    // 32-bit partition arithmetic: every product is at most T*P <= share*P*P
+    if ((uint64_t)share * P * P >= (1ull << 32)) return pl;
     cap = share;  // stage buffers only as large as a share
     pl.K = (int)k;
     pl.U = (int)U;
@@ -921,13 +994,14 @@ PPlan plan_persistent(int64_t batch, int64_t filters, int64_t spatial, const Dev
     pl.maxj = (int)((cap - 1) / NK + 2);
     pl.stages = stages;
     pl.smem = K::smem_bytes(stages, pl.cap_units, pl.U, pl.maxj);
-    pl.ok = pl.smem <= (size_t)ds->max_smem_optin;
+    pl.ok = pl.smem <= per_cta;
+    pl.ctas_per_sm = ctas;
     return pl;
 }
 
 int stages_from_env() {
     const char *e = getenv("DNB_BN_STAGES");
-    int s = e ? atoi(e) : 2;
+    int s = e ? atoi(e) : 3;
     return s < 2 ? 2 : (s > kMaxStages ? kMaxStages : s);
 }
 
@@ -943,7 +1017,9 @@ dnb_status launch_persistent(const PPlan &pl, PArgs &a, int act, cudaStream_t st
         DNB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem));
         int per_sm = 0;
         DNB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kPThreads, pl.smem));
-        if (per_sm < 1) return fail(DNB_ERR_UNSUPPORTED, "%s: persistent kernel does not fit an SM", what);
+        if (per_sm < pl.ctas_per_sm)
+            return fail(DNB_ERR_UNSUPPORTED, "%s: %d CTAs of the persistent kernel fit an SM, the plan needs %d",
+                        what, per_sm, pl.ctas_per_sm);
         void *args[] = {&a};
         DNB_CUDA(cudaLaunchCooperativeKernel((const void *)kern, dim3((unsigned)pl.P), dim3(kPThreads), args, pl.smem,
                                              stream));
@@ -976,7 +1052,17 @@ dnb_status prepare_persistent(int64_t batch, int64_t filters, int64_t spatial, c
     a->f_u4 = FastDiv((uint32_t)(pl.U / 4));
     a->f_nk = FastDiv((uint32_t)a->NK);
     a->f_k = FastDiv((uint32_t)pl.K);
+    a->f_p = FastDiv((uint32_t)pl.P);
+    a->T_full = (uint32_t)pl.cg * (uint32_t)a->NK;
+    a->T_last = (uint32_t)(filters - (int64_t)(pl.G - 1) * pl.cg) * (uint32_t)a->NK;
+    a->f_tfull = FastDiv(a->T_full);
+    a->f_tlast = FastDiv(a->T_last);
     a->denom = (float)(spatial * batch);
+    // dividing by a power of two equals multiplying by its exact reciprocal
+    int e2 = 0;
+    const float fr = frexpf(a->denom, &e2);
+    a->denom_pow2 = fr == 0.5f;
+    a->inv_denom = 1.0f / a->denom;
     a->rec = static_cast<float2 *>(ws->scratch);
     a->sync = ws->sync;
     a->err = ds->error_word;
@@ -989,6 +1075,14 @@ dnb_status prepare_persistent(int64_t batch, int64_t filters, int64_t spatial, c
 }  // namespace dnb
 
 using namespace dnb;
+
+#ifdef DNB_PHASE_TIMING
+extern "C" dnb_status dnb_debug_phase_times(unsigned long long *host, size_t count) {
+    DNB_CUDA(cudaDeviceSynchronize());
+    DNB_CUDA(cudaMemcpyFromSymbol(host, g_phase_ts, count * sizeof(unsigned long long)));
+    return DNB_OK;
+}
+#endif
 
 extern "C" {
 

@@ -44,6 +44,8 @@ struct DeviceState {
     int device = -1;
     int sm_count = 0;
     int max_smem_optin = 0;        // bytes of dynamic shared memory a CTA may opt into
+    int smem_per_sm = 0;           // shared memory of one SM
+    int smem_reserved = 0;         // shared memory the system reserves per CTA
     unsigned *error_word = nullptr;  // device: DEVERR_* bits, sticky until dnb_check_device_error
     unsigned *abort_flag = nullptr;  // device: set with the error word, makes other waiters give up
 };

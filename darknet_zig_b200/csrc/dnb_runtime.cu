@@ -30,6 +30,8 @@ dnb_status init_device(int device) {
     DNB_CUDA(cudaSetDevice(device));
     DNB_CUDA(cudaDeviceGetAttribute(&ds.sm_count, cudaDevAttrMultiProcessorCount, device));
     DNB_CUDA(cudaDeviceGetAttribute(&ds.max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device));
+    DNB_CUDA(cudaDeviceGetAttribute(&ds.smem_per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, device));
+    DNB_CUDA(cudaDeviceGetAttribute(&ds.smem_reserved, cudaDevAttrReservedSharedMemoryPerBlock, device));
     unsigned *words = nullptr;
     DNB_CUDA(cudaMalloc(&words, 2 * sizeof(unsigned)));
     DNB_CUDA(cudaMemset(words, 0, 2 * sizeof(unsigned)));

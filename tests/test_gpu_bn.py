@@ -273,30 +273,52 @@ def test_unfused_reference_sequence_matches_fused(cuda, oracle, shape):
 
 def test_syncbn_split_path_two_shards_on_one_gpu(cuda):
     """Split sync-BN API: two half-batch shards, partials combined as an all-gather would,
-    equal the single-shard statistics of the whole batch."""
+    give the statistics and outputs of the whole batch in one shard."""
+    from darknet_zig_b200._lib import call
+
     B, C, S = 16, 24, 196
     x, gamma, beta, delta, _, _ = make_inputs((B, C, S), seed=31)
     h = B // 2
+    g_d, b_d = dev(gamma), dev(beta)  # held: the ABI takes raw pointers
     xs = [dev(x[: h * C * S]), dev(x[h * C * S:])]
     parts = [torch.zeros(C, 2, dtype=torch.float64, device="cuda") for _ in range(2)]
-    from darknet_zig_b200._lib import call
+    stream = torch.cuda.current_stream().cuda_stream
     for xi, p in zip(xs, parts):
-        call("syncbn_forward_partials", xi.data_ptr(), h, C, S, p.data_ptr(), torch.cuda.current_stream().cuda_stream)
+        call("syncbn_forward_partials", xi.data_ptr(), h, C, S, p.data_ptr(), stream)
     gathered = torch.stack(parts).contiguous()
-    m_full = torch.zeros(C, device="cuda")
-    v_full = torch.zeros(C, device="cuda")
+    m_full, v_full = torch.zeros(C, device="cuda"), torch.zeros(C, device="cuda")
     y_full = torch.empty(B * C * S, device="cuda")
-    gpu.bnActForwardTrain(dev(x), y_full, None, B, C, S, dev(gamma), dev(beta), m_full, v_full,
-                          torch.zeros(C, device="cuda"), torch.zeros(C, device="cuda"), gpu.LEAKY)
+    gpu.bnActForwardTrain(dev(x), y_full, None, B, C, S, g_d, b_d, m_full, v_full, torch.zeros(C, device="cuda"),
+                          torch.zeros(C, device="cuda"), gpu.LEAKY)
     for i, xi in enumerate(xs):
         y = torch.empty(h * C * S, device="cuda")
-        m = torch.zeros(C, device="cuda")
-        v = torch.zeros(C, device="cuda")
+        m, v, rm, rv = (torch.zeros(C, device="cuda") for _ in range(4))
         call("syncbn_forward_apply", xi.data_ptr(), y.data_ptr(), None, h, C, S, gathered.data_ptr(), 2,
-             dev(gamma).data_ptr(), dev(beta).data_ptr(), m.data_ptr(), v.data_ptr(),
-             torch.zeros(C, device="cuda").data_ptr(), torch.zeros(C, device="cuda").data_ptr(), gpu.LEAKY,
-             torch.cuda.current_stream().cuda_stream)
+             g_d.data_ptr(), b_d.data_ptr(), m.data_ptr(), v.data_ptr(), rm.data_ptr(), rv.data_ptr(), gpu.LEAKY,
+             stream)
         assert_close(host(m), host(m_full), "sync mean", rtol=1e-5, atol=1e-6)
         assert_close(host(v), host(v_full), "sync variance", rtol=1e-5, atol=1e-6)
         half = slice(i * h * C * S, (i + 1) * h * C * S)
         assert_close(host(y), host(y_full)[half], "sync y", rtol=1e-5, atol=1e-5)
+    # backward: partial sums of both shards, summed as an all-reduce would
+    d_d = dev(delta)
+    ds = [d_d[: h * C * S], d_d[h * C * S:]]
+    bparts = [torch.zeros(C, 2, dtype=torch.float64, device="cuda") for _ in range(2)]
+    for xi, di, p in zip(xs, ds, bparts):
+        call("syncbn_backward_partials", xi.data_ptr(), None, di.data_ptr(), h, C, S, g_d.data_ptr(), b_d.data_ptr(),
+             m_full.data_ptr(), v_full.data_ptr(), gpu.LEAKY, p.data_ptr(), stream)
+    red = (bparts[0] + bparts[1]).contiguous()
+    dx_full = torch.empty_like(y_full)
+    bu, su, md, vd = (torch.zeros(C, device="cuda") for _ in range(4))
+    gpu.bnActBackward(dev(x), None, d_d, dx_full, B, C, S, g_d, b_d, m_full, v_full, bu, su, md, vd, gpu.LEAKY)
+    for i, (xi, di) in enumerate(zip(xs, ds)):
+        dx = torch.empty(h * C * S, device="cuda")
+        bu2, su2, md2, vd2 = (torch.zeros(C, device="cuda") for _ in range(4))
+        call("syncbn_backward_apply", xi.data_ptr(), None, di.data_ptr(), dx.data_ptr(), h, C, S, B * S,
+             red.data_ptr(), g_d.data_ptr(), b_d.data_ptr(), m_full.data_ptr(), v_full.data_ptr(), bu2.data_ptr(),
+             su2.data_ptr(), md2.data_ptr(), vd2.data_ptr(), gpu.LEAKY, stream)
+        for got, want, name in ((bu2, bu, "bias_updates"), (su2, su, "scale_updates"), (md2, md, "mean_delta"),
+                                (vd2, vd, "variance_delta")):
+            assert_close(host(got), host(want), f"sync {name}", rtol=1e-5, atol=1e-5)
+        half = slice(i * h * C * S, (i + 1) * h * C * S)
+        assert_close(host(dx), host(dx_full)[half], "sync dx", rtol=1e-4, atol=1e-5)

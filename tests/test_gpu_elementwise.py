@@ -205,10 +205,12 @@ def test_softmax_and_cross_entropy(cuda, oracle, rows, classes):
     assert_close(host(cost), np.array([want_cost], np.float32), "cost", rtol=1e-5, atol=1e-5)
 
 
-@pytest.mark.parametrize("temp,stride,groups", [(2.0, 1, 1), (1.0, 2, 3)])
+@pytest.mark.parametrize("temp,stride,groups", [(2.0, 1, 1), (1.0, 1, 3), (1.0, 2, 2), (0.5, 3, 3)])
 def test_softmax_strided_groups(cuda, oracle, temp, stride, groups):
+    """Grouped and interleaved rows (blas.zig:210-212): with stride s the s groups of a
+    batch item interleave (group_offset 1); with stride 1 they are consecutive."""
     batch, n = 4, 50
-    batch_offset = n * groups * stride
+    batch_offset = n * groups
     size = batch * batch_offset
     x = synth.normal(21, (size,), 0, 1)
     out = dev(np.zeros(size, np.float32))
