@@ -9,24 +9,15 @@
 // forward (read x, write y) and 12 B/elem backward (read delta and x, write dx).
 //
 // The obstacle is the per-channel reduction that must finish before any element can be
-// written. The persistent kernel here removes the second read:
-//   * one CTA per SM (cooperative launch, so every CTA is resident) owns ~200 KB of shared
-//     memory split into two stage buffers;
-//   * channels are processed in groups sized so that a group's units (contiguous runs of a
-//     plane) fill every CTA's stage buffer once;
-//   * a CTA pulls its share of group g into shared memory with 1-D bulk TMA copies,
-//     reduces it per channel, publishes one partial record per (CTA, channel), and
-//     arrives on a per-group counter in global memory;
-//   * once all CTAs have arrived it merges the channel's records (Chan's parallel
-//     variance formula, fp64), and writes the group's outputs straight from shared memory.
-//     The copy of group g+1 is in flight during that wait, so HBM stays busy.
-// Every wait is bounded: a CTA that gives up sets the device error word, waits (bounded)
-// for its own copies, and exits; the host reports DNB_ERR_TIMEOUT.
+// written. The persistent kernel below keeps the second read off HBM: channels are taken
+// in groups sized to a slice of the 126 MB L2, half the CTAs stream group g+1 and reduce
+// it while the other half merge group g's partials and write its outputs, re-reading the
+// inputs from L2 (see the comment above k_bn_persistent). Every wait is bounded: a CTA
+// that gives up sets the device error word and exits; the host reports DNB_ERR_TIMEOUT.
 //
-// Shapes the persistent kernel does not take (spatial % 4 != 0, a channel larger than the
-// whole grid's shared memory, unaligned pointers) run the generic three-launch path below,
-// which also implements the split sync-BN entry points: per-channel partials ->
-// (caller's collective) -> finalize + apply.
+// Shapes the persistent kernel does not take (spatial % 4 != 0, unaligned pointers) run
+// the generic three-launch path below, which also implements the split sync-BN entry
+// points: per-channel partials -> (caller's collective) -> finalize + apply.
 //
 // Per-element arithmetic follows the reference CPU code (blas.zig:137-204) operation by
 // operation without fused roundings (--fmad=false), so given the same per-channel
@@ -430,13 +421,95 @@ dnb_status generic_bwd_apply(const GGeom &g, const float *x, const float *y, con
 }
 
 // ======================================================================================
-// persistent fused kernel
+// persistent fused kernel: a grid-level pipeline over channel groups, TMA-staged
 // ======================================================================================
+//
+// The channels are processed in groups. One cooperative grid, two roles (even / odd CTAs,
+// so every SM runs one of each):
+//   stats CTAs  copy their balanced share of group g from HBM into shared memory with 1-D
+//               TMA bulk copies (double-buffered: group g+1 is in flight while g is
+//               reduced), reduce it per channel segment (a share spans at most two
+//               channels), publish one partial record per (CTA, segment, warp), and count
+//               themselves in stats_done[g];
+//   apply CTAs  once stats_done[g] is complete, bulk-copy the same units -- now resident in
+//               L2, where the stats copies left them -- into their own shared memory,
+//               merge the records of their share's channels (fp64, one L2 round trip,
+//               overlapping the copy), write the outputs with streaming stores from shared
+//               memory, and count themselves in apply_done[g].
+// The TMA engine keeps the bytes in flight, so neither role needs registers or warps to
+// cover HBM latency, and every input byte crosses HBM once. Stats CTAs refill a buffer
+// with group h only once apply_done[h - depth] is complete, bounding what sits in L2.
+// The only waits are a stats CTA on the apply of an earlier group and an apply CTA on the
+// stats of the group it is about to copy: no cycle. Every wait is bounded (the kernel then
+// sets the device error word, waits for its own copies, and returns).
 
-constexpr int kPThreads = 256;
-constexpr int kPMinBlocks = 2;  // CTAs per SM the register budget is sized for
-constexpr int kMaxStages = 3;
+constexpr int kLThreads = 512;
+constexpr int kLWarps = kLThreads / 32;
 
+// Everything the persistent kernel needs, by value. Partition arithmetic is 32-bit with
+// FastDiv: the plan guarantees T * max(Ps, Pa) < 2^32.
+struct PArgs {
+    int64_t C, S;
+    int N, K, U, NK;          // batch, pieces per plane, unit floats (S/K), units per channel
+    int cg, G;                // channels per group, groups
+    int Ps, Pa, depth;        // stats CTAs, apply CTAs, groups resident in L2 at once (>= 3)
+    int cap_units;            // units one shared-memory buffer holds per tensor
+    uint32_t T_full, T_last;  // units in a group (every group but the last / the last)
+    FastDiv f_u4, f_nk, f_k, f_ps, f_pa, f_tfull, f_tlast;
+    float denom;              // batch*spatial as f32 (normalize_delta's denominator)
+    float inv_denom;          // 1/denom, used only when denom is a power of two (then exact)
+    int denom_pow2;
+    // tensors: fwd uses t0 = x; bwd uses t0 = delta, t1 = x, t2 = y (optional)
+    const float *t0, *t1, *t2;
+    float *out, *xnorm;
+    const float *scales, *biases;
+    float *mean, *var, *rmean, *rvar;
+    const float *mean_in, *var_in;
+    float *bias_upd, *scale_upd, *mean_delta, *var_delta;
+    int act;
+    float4 *rec;              // [G][Ps][2 segments]
+    uint32_t step_q, step_r;  // kLThreads float4s = step_q units + step_r float4s
+    unsigned *sync;           // [0] epoch, then 2 banks of {stats_done[kMaxGroups], apply_done[kMaxGroups]}
+    unsigned *err, *abort_flag;
+    unsigned long long wait_ns;
+};
+
+// Share of CTA p of a role with `parts` CTAs in group g: units [t0, t1) of the group's T,
+// in at most two channel segments (the plan keeps shares no longer than a channel).
+struct Share {
+    uint32_t c0, T, t0, t1, bnd;  // bnd: first unit of the second segment
+    int cfirst, nseg;
+};
+__device__ __forceinline__ Share share_of(const PArgs &a, int g, int p, const FastDiv &parts) {
+    Share s;
+    s.c0 = (uint32_t)g * (uint32_t)a.cg;
+    s.T = g == a.G - 1 ? a.T_last : a.T_full;
+    s.t0 = parts.div((uint32_t)p * s.T);
+    s.t1 = parts.div((uint32_t)(p + 1) * s.T);
+    s.cfirst = (int)a.f_nk.div(s.t0);
+    s.bnd = (uint32_t)(s.cfirst + 1) * (uint32_t)a.NK;
+    s.nseg = s.t1 <= s.t0 ? 0 : (s.t1 <= s.bnd ? 1 : 2);
+    return s;
+}
+// The CTA (of a role with `parts` CTAs) that owns unit t of group g.
+__device__ __forceinline__ int owner_of(const PArgs &a, int g, uint32_t t, int parts) {
+    const FastDiv &fd = g == a.G - 1 ? a.f_tlast : a.f_tfull;
+    return (int)fd.div((t + 1) * (uint32_t)parts - 1);
+}
+
+// Element offset and segment of float4 i of a share.
+__device__ __forceinline__ void locate(const PArgs &a, const Share &sh, uint32_t i, int64_t &off, int &seg) {
+    uint32_t u, r;
+    a.f_u4.divmod(i, u, r);
+    const uint32_t t = sh.t0 + u;
+    seg = t >= sh.bnd ? 1 : 0;
+    const uint32_t cl = (uint32_t)(sh.cfirst + seg);
+    uint32_t n, k;
+    a.f_k.divmod(t - cl * (uint32_t)a.NK, n, k);
+    off = ((int64_t)n * a.C + sh.c0 + cl) * a.S + (int64_t)k * a.U + 4 * (int64_t)r;
+}
+
+// ---- TMA 1-D bulk copies and mbarriers (no multicast) ----
 __device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
 __device__ __forceinline__ void mbar_init(uint64_t *bar, unsigned count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
@@ -457,69 +530,12 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, unsigned parity) {
         : "memory");
     return ok != 0;
 }
-// 1-D bulk copy global -> this CTA's shared memory, completing on `bar` (no multicast).
+// global -> this CTA's shared memory, completing on `bar`
 __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, unsigned bytes, uint64_t *bar) {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
                      smem_u32(dst)),
                  "l"(src), "r"(bytes), "r"(smem_u32(bar))
                  : "memory");
-}
-
-// Everything the persistent kernel needs, by value. All partition arithmetic is 32-bit
-// with FastDiv: the plan guarantees cap_units * P * P < 2^32, which bounds every product
-// below (p*T, (t+1)*P with T <= cap_units*P).
-struct PArgs {
-    // geometry
-    int64_t C, S;
-    int N, K, U, NK;       // batch, units per plane, unit floats, units per channel
-    int cg, G, P;          // channels per group, groups, CTAs
-    int cap_units, maxj, stages;
-    uint32_t T_full, T_last;  // units in a group (every group but the last / the last)
-    FastDiv f_u4, f_nk, f_k, f_p, f_tfull, f_tlast;
-    float denom;           // batch*spatial as f32 (normalize_delta's denominator)
-    float inv_denom;       // 1/denom, used only when denom is a power of two (then exact)
-    int denom_pow2;
-    // tensors: fwd uses t0 = x; bwd uses t0 = delta, t1 = x, t2 = y (optional)
-    const float *t0, *t1, *t2;
-    float *out, *xnorm;
-    // per-channel parameters and outputs
-    const float *scales, *biases;
-    float *mean, *var, *rmean, *rvar;
-    const float *mean_in, *var_in;
-    float *bias_upd, *scale_upd, *mean_delta, *var_delta;
-    int act;
-    // workspace
-    float2 *rec;           // [G][P][maxj]
-    unsigned *sync;        // [0] epoch, then 2 banks of kMaxGroups counters
-    unsigned *err, *abort_flag;
-    unsigned long long wait_ns;
-};
-
-struct UnitEntry {
-    long long goff;  // element offset of the unit in the tensors
-    int j;           // channel slot within the CTA's share
-    int pad;
-};
-
-// Share of CTA p in group g: units [t0, t1) of the group's T (channel base c0).
-struct Share {
-    uint32_t c0, T, t0, t1;
-    int cfirst, clast;  // local channel indices touched (inclusive); cfirst > clast when empty
-};
-__device__ __forceinline__ Share share_of(const PArgs &a, int g, int p) {
-    Share s;
-    s.c0 = (uint32_t)g * (uint32_t)a.cg;
-    s.T = g == a.G - 1 ? a.T_last : a.T_full;
-    s.t0 = a.f_p.div((uint32_t)p * s.T);
-    s.t1 = a.f_p.div((uint32_t)(p + 1) * s.T);
-    s.cfirst = (int)a.f_nk.div(s.t0);
-    s.clast = s.t1 > s.t0 ? (int)a.f_nk.div(s.t1 - 1) : s.cfirst - 1;
-    return s;
-}
-// The CTA that owns unit t of group g: the largest p with floor(p*T/P) <= t.
-__device__ __forceinline__ int owner_of(const PArgs &a, int g, uint32_t t) {
-    const FastDiv &fd = g == a.G - 1 ? a.f_tlast : a.f_tfull;
-    return (int)fd.div((t + 1) * (uint32_t)a.P - 1);
 }
 
 __device__ __forceinline__ float div_denom(float v, const PArgs &a) {
@@ -530,316 +546,49 @@ __device__ __forceinline__ float bn_dx_p(float gval, float x, const BwdParam &p,
     return (gval * p.g) * p.inv2 + div_denom(p.vd * 2.0f * (x - p.m), a) + p.mdd;
 }
 
-template <bool BWD, int A, bool HASY>
-struct PKernel {
-    static constexpr int NT = BWD ? (HASY ? 3 : 2) : 1;  // tensors staged per unit
-
-    struct Smem {
-        float *buf;          // [stages][NT][cap_units*U]
-        uint64_t *bars;      // [stages]
-        UnitEntry *units;    // [stages][cap_units]
-        float *ptab;         // apply records of the current group: [maxj][8]
-        float *red;          // 64 floats
-        int *flag;
-    };
-
-    // Byte offsets of the regions of dynamic shared memory, each 16-byte aligned.
-    struct Layout {
-        size_t bars, units, ptab, red, flag, total;
-    };
-    __host__ __device__ static size_t up16(size_t b) { return (b + 15) & ~(size_t)15; }
-    __host__ __device__ static Layout layout(int stages, int cap_units, int U, int maxj) {
-        Layout l;
-        l.bars = up16((size_t)stages * NT * cap_units * U * sizeof(float));
-        l.units = up16(l.bars + kMaxStages * sizeof(uint64_t));
-        l.ptab = up16(l.units + (size_t)stages * cap_units * sizeof(UnitEntry));
-        l.red = up16(l.ptab + (size_t)maxj * 8 * sizeof(float));
-        l.flag = up16(l.red + 64 * sizeof(float));
-        l.total = l.flag + 16;
-        return l;
+// Chan et al.'s combination of two (count, mean, M2) summaries.
+__device__ __forceinline__ void chan_merge(float &n, float &m, float &q, float nb, float mb, float qb) {
+    const float nn = n + nb;
+    if (nn > 0.0f) {
+        const float d = mb - m;
+        const float f = nb / nn;
+        m = m + d * f;
+        q = q + qb + d * d * n * f;
+        n = nn;
     }
-    __device__ static Smem carve(const PArgs &a, unsigned char *raw) {
-        const Layout l = layout(a.stages, a.cap_units, a.U, a.maxj);
-        Smem s;
-        s.buf = reinterpret_cast<float *>(raw);
-        s.bars = reinterpret_cast<uint64_t *>(raw + l.bars);
-        s.units = reinterpret_cast<UnitEntry *>(raw + l.units);
-        s.ptab = reinterpret_cast<float *>(raw + l.ptab);
-        s.red = reinterpret_cast<float *>(raw + l.red);
-        s.flag = reinterpret_cast<int *>(raw + l.flag);
-        return s;
-    }
-    __host__ static size_t smem_bytes(int stages, int cap_units, int U, int maxj) {
-        return layout(stages, cap_units, U, maxj).total;
-    }
+}
 
-    __device__ static float *tensor_buf(const PArgs &a, const Smem &s, int stage, int t) {
-        return s.buf + ((size_t)stage * NT + t) * a.cap_units * a.U;
+// Per-thread running moments of one segment, shifted by the first value the thread saw.
+struct Moments {
+    float shift = 0.0f, s1 = 0.0f, s2 = 0.0f, n = 0.0f;
+    __device__ __forceinline__ void add4(float4 v) {
+        if (n == 0.0f) shift = v.x;
+        const float d0 = v.x - shift, d1 = v.y - shift, d2 = v.z - shift, d3 = v.w - shift;
+        s1 += (d0 + d1) + (d2 + d3);
+        s2 += (d0 * d0 + d1 * d1) + (d2 * d2 + d3 * d3);
+        n += 4.0f;
     }
-
-    // Issue the copies of group g into `stage` (warp 0; lane 0 arms the barrier first).
-    __device__ static void issue(const PArgs &a, const Smem &s, int g, int stage) {
-        if (threadIdx.x >= 32) return;
-        const Share sh = share_of(a, g, blockIdx.x);
-        const int n_units = (int)(sh.t1 - sh.t0);
-        const unsigned unit_bytes = (unsigned)a.U * sizeof(float);
-        if (threadIdx.x == 0) {
-            fence_proxy_async();
-            mbar_arrive_expect_tx(&s.bars[stage], (unsigned)(n_units * NT) * unit_bytes);
-        }
-        __syncwarp();
-        const float *src[3] = {a.t0, a.t1, a.t2};
-        for (int u = threadIdx.x; u < n_units; u += 32) {
-            const uint32_t t = sh.t0 + u;
-            uint32_t cl, rem, n, k;
-            a.f_nk.divmod(t, cl, rem);
-            a.f_k.divmod(rem, n, k);
-            const int64_t c = (int64_t)sh.c0 + cl;
-            const int64_t goff = ((int64_t)n * a.C + c) * a.S + (int64_t)k * a.U;
-            s.units[stage * a.cap_units + u] = UnitEntry{goff, (int)cl - sh.cfirst, 0};
+    // warp-wide (count, mean, M2), valid in every lane
+    __device__ __forceinline__ float4 warp_summary() const {
+        float m = n > 0.0f ? shift + s1 / n : 0.0f;
+        float q = n > 0.0f ? s2 - s1 * (s1 / n) : 0.0f;
+        if (q < 0.0f) q = 0.0f;
+        float c = n;
 #pragma unroll
-            for (int tt = 0; tt < NT; ++tt)
-                bulk_g2s(tensor_buf(a, s, stage, tt) + (size_t)u * a.U, src[tt] + goff, unit_bytes, &s.bars[stage]);
+        for (int o = 16; o > 0; o >>= 1) {
+            const float cb = __shfl_xor_sync(0xffffffffu, c, o);
+            const float mb = __shfl_xor_sync(0xffffffffu, m, o);
+            const float qb = __shfl_xor_sync(0xffffffffu, q, o);
+            chan_merge(c, m, q, cb, mb, qb);
         }
-    }
-
-    // Wait (bounded) for the copies of `stage` with the given phase parity.
-    __device__ static bool wait_copies(const PArgs &a, const Smem &s, int stage, unsigned parity) {
-        const unsigned long long deadline = global_ns() + a.wait_ns;
-        unsigned it = 0;
-        while (!mbar_try_wait(&s.bars[stage], parity)) {
-            if ((++it & 63u) == 0 && global_ns() > deadline) {
-                atomicOr(a.err, DEVERR_WAIT_COPY);
-                atomicExch(a.abort_flag, 1u);
-                return false;
-            }
-        }
-        return true;
-    }
-
-    // Per-channel partial of one share segment (the whole block; result valid in thread 0).
-    __device__ static float2 segment_stats(const PArgs &a, const Smem &s, int stage, int ua, int ub, int64_t c) {
-        const int q0 = ua * (a.U >> 2), q1 = ub * (a.U >> 2);  // float4 range in the stage buffer
-        const float4 *b0 = reinterpret_cast<const float4 *>(tensor_buf(a, s, stage, 0));
-        if constexpr (!BWD) {
-            // one pass: per-thread sums shifted by the thread's first element, then the block
-            // merges (count, mean, M2) of its threads (Chan et al.)
-            float shift = 0.0f, s1 = 0.0f, s2 = 0.0f, nt = 0.0f;
-            if (q0 + (int)threadIdx.x < q1) shift = b0[q0 + threadIdx.x].x;
-            for (int q = q0 + threadIdx.x; q < q1; q += kPThreads) {
-                const float4 v = b0[q];
-                const float d0 = v.x - shift, d1 = v.y - shift, d2 = v.z - shift, d3 = v.w - shift;
-                s1 += (d0 + d1) + (d2 + d3);
-                s2 += (d0 * d0 + d1 * d1) + (d2 * d2 + d3 * d3);
-                nt += 4.0f;
-            }
-            const float cnt = (float)((q1 - q0) * 4);
-            const float mt = nt > 0.0f ? shift + s1 / nt : 0.0f;
-            float m2t = nt > 0.0f ? s2 - s1 * (s1 / nt) : 0.0f;
-            if (m2t < 0.0f) m2t = 0.0f;
-            const float mr = block_sum<kPThreads>(nt > 0.0f ? nt * shift + s1 : 0.0f, s.red) / cnt;
-            const float dm = mt - mr;
-            const float m2 = block_sum<kPThreads>(nt > 0.0f ? m2t + nt * dm * dm : 0.0f, s.red);
-            return make_float2(mr, m2);
-        } else {
-            const float4 *bx = reinterpret_cast<const float4 *>(tensor_buf(a, s, stage, 1));
-            const float4 *by = reinterpret_cast<const float4 *>(tensor_buf(a, s, stage, NT - 1));
-            BwdParam p;
-            p.m = a.mean_in[c];
-            p.inv = 1.0f / (sqrtf(a.var_in[c]) + 0.000001f);
-            p.g = a.scales[c];
-            p.b = a.biases[c];
-            float s1 = 0.0f, s2 = 0.0f;
-            for (int q = q0 + threadIdx.x; q < q1; q += kPThreads) {
-                const float4 d = b0[q], xv = bx[q];
-                const float4 yv = HASY ? by[q] : xv;
-                const float g0 = bn_grad1<A, HASY>(d.x, xv.x, yv.x, p, a.act);
-                const float g1 = bn_grad1<A, HASY>(d.y, xv.y, yv.y, p, a.act);
-                const float g2 = bn_grad1<A, HASY>(d.z, xv.z, yv.z, p, a.act);
-                const float g3 = bn_grad1<A, HASY>(d.w, xv.w, yv.w, p, a.act);
-                s1 += (g0 + g1) + (g2 + g3);
-                s2 += (g0 * (xv.x - p.m) + g1 * (xv.y - p.m)) + (g2 * (xv.z - p.m) + g3 * (xv.w - p.m));
-            }
-            return block_sum2<kPThreads>(s1, s2, s.red);
-        }
-    }
-
-    // Partials of every channel segment of this CTA's share of group g -> records.
-    __device__ static void stats(const PArgs &a, const Smem &s, int g, int stage) {
-        const Share sh = share_of(a, g, blockIdx.x);
-        for (int cl = sh.cfirst; cl <= sh.clast; ++cl) {
-            uint32_t ua = (uint32_t)cl * a.NK, ub = ua + a.NK;
-            if (ua < sh.t0) ua = sh.t0;
-            if (ub > sh.t1) ub = sh.t1;
-            const float2 r = segment_stats(a, s, stage, (int)(ua - sh.t0), (int)(ub - sh.t0), (int64_t)sh.c0 + cl);
-            if (threadIdx.x == 0)
-                a.rec[((int64_t)g * a.P + blockIdx.x) * a.maxj + (cl - sh.cfirst)] = r;
-        }
-    }
-
-    // Publish this CTA's records of group g: fence, then one arrival on the group counter.
-    __device__ static void arrive(const PArgs &a, unsigned *cnt, int g, bool last_group, unsigned epoch) {
-        if (threadIdx.x == 0) {
-            __threadfence();
-            const unsigned prev = atomicAdd(&cnt[g], 1u);
-            // every CTA read the epoch before its first arrival: the last one of the last
-            // group advances it for the next launch
-            if (last_group && prev == (unsigned)a.P - 1) atomicExch(&a.sync[0], epoch + 1);
-        }
-    }
-
-    // Wait (bounded) until every CTA has arrived on group g; block-uniform result.
-    __device__ static bool wait_group(const PArgs &a, const Smem &s, unsigned *cnt, int g) {
-        if (threadIdx.x == 0) {
-            int ok = 1;
-            const unsigned long long deadline = global_ns() + a.wait_ns;
-            while (ld_acquire_gpu(&cnt[g]) < (unsigned)a.P) {
-                if (ld_volatile(a.abort_flag)) {
-                    ok = 0;
-                    break;
-                }
-                if (global_ns() > deadline) {
-                    atomicOr(a.err, DEVERR_WAIT_BARRIER);
-                    atomicExch(a.abort_flag, 1u);
-                    ok = 0;
-                    break;
-                }
-                __nanosleep(32);
-            }
-            *s.flag = ok;
-        }
-        __syncthreads();
-        return *s.flag != 0;
-    }
-
-    // Merge the records of every channel this CTA's share of group g touches and build the
-    // apply table; the CTA owning a channel's first unit writes the per-channel outputs.
-    __device__ static void finalize(const PArgs &a, const Smem &s, int g) {
-        const Share sh = share_of(a, g, blockIdx.x);
-        const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-        for (int cl = sh.cfirst + warp; cl <= sh.clast; cl += kPThreads / 32) {
-            const int64_t c = (int64_t)sh.c0 + cl;
-            const uint32_t ua = (uint32_t)cl * a.NK, ub = ua + a.NK;
-            const int plo = owner_of(a, g, ua), phi = owner_of(a, g, ub - 1);
-            const bool write = plo == (int)blockIdx.x;
-            float *out = s.ptab + (cl - sh.cfirst) * 8;
-            // CTAs between plo and phi with no unit of this channel (a group with fewer
-            // units than CTAs) wrote no record for it: skip them
-            if constexpr (!BWD) {
-                double cm = 0.0, n_r = 0.0, m_r = 0.0, q_r = 0.0;
-                bool have = false;
-                for (int p = plo + lane; p <= phi; p += 32) {
-                    const Share o = share_of(a, g, p);
-                    const uint32_t lo = ua > o.t0 ? ua : o.t0, hi = ub < o.t1 ? ub : o.t1;
-                    if (hi <= lo) continue;
-                    const float2 r = __ldcg(&a.rec[((int64_t)g * a.P + p) * a.maxj + (cl - o.cfirst)]);
-                    const double nr = (double)((hi - lo) * (uint32_t)a.U);
-                    cm += nr * (double)r.x;
-                    if (p + 32 > phi) {  // the common case: one record per lane
-                        n_r = nr;
-                        m_r = r.x;
-                        q_r = r.y;
-                        have = true;
-                    }
-                }
-                const double n = (double)a.NK * a.U;
-                const double mu = warp_sum(cm) / n;
-                double m2 = 0.0;
-                if (phi - plo < 32) {
-                    if (have) m2 = q_r + n_r * (m_r - mu) * (m_r - mu);
-                } else {
-                    for (int p = plo + lane; p <= phi; p += 32) {
-                        const Share o = share_of(a, g, p);
-                        const uint32_t lo = ua > o.t0 ? ua : o.t0, hi = ub < o.t1 ? ub : o.t1;
-                        if (hi <= lo) continue;
-                        const float2 r = __ldcg(&a.rec[((int64_t)g * a.P + p) * a.maxj + (cl - o.cfirst)]);
-                        const double d = (double)r.x - mu;
-                        m2 += (double)r.y + (double)((hi - lo) * (uint32_t)a.U) * d * d;
-                    }
-                }
-                m2 = warp_sum(m2);
-                if (lane == 0) {
-                    const FwdClose f = fwd_close(mu, m2, n);
-                    if (write) {
-                        a.mean[c] = f.m;
-                        a.var[c] = f.var;
-                        a.rmean[c] = rolling(a.rmean[c], f.m);
-                        a.rvar[c] = rolling(a.rvar[c], f.var);
-                    }
-                    out[0] = f.m;
-                    out[1] = f.inv;
-                    out[2] = a.scales[c];
-                    out[3] = a.biases[c];
-                }
-            } else {
-                double s1 = 0.0, s2 = 0.0;
-                for (int p = plo + lane; p <= phi; p += 32) {
-                    const Share o = share_of(a, g, p);
-                    const uint32_t lo = ua > o.t0 ? ua : o.t0, hi = ub < o.t1 ? ub : o.t1;
-                    if (hi <= lo) continue;
-                    const float2 r = __ldcg(&a.rec[((int64_t)g * a.P + p) * a.maxj + (cl - o.cfirst)]);
-                    s1 += (double)r.x;
-                    s2 += (double)r.y;
-                }
-                s1 = warp_sum(s1);
-                s2 = warp_sum(s2);
-                if (lane == 0) {
-                    const BwdParam bp = bwd_close(s1, s2, a.mean_in[c], a.var_in[c], a.scales[c], a.biases[c],
-                                                  a.denom, a.bias_upd, a.scale_upd, a.mean_delta, a.var_delta, c,
-                                                  write);
-                    *reinterpret_cast<BwdParam *>(out) = bp;
-                }
-            }
-        }
-        __syncthreads();
-    }
-
-    __device__ static void apply(const PArgs &a, const Smem &s, int g, int stage) {
-        const Share sh = share_of(a, g, blockIdx.x);
-        const uint32_t u4 = (uint32_t)a.U >> 2;
-        const uint32_t n4 = (sh.t1 - sh.t0) * u4;
-        const float4 *b0 = reinterpret_cast<const float4 *>(tensor_buf(a, s, stage, 0));
-        const UnitEntry *ut = s.units + stage * a.cap_units;
-        if constexpr (!BWD) {
-            for (uint32_t i = threadIdx.x; i < n4; i += kPThreads) {
-                uint32_t u, r;
-                a.f_u4.divmod(i, u, r);
-                const UnitEntry e = ut[u];
-                const float4 p = *reinterpret_cast<const float4 *>(s.ptab + e.j * 8);
-                const float4 v = b0[i];
-                const int64_t off = e.goff + 4 * (int64_t)r;
-                if (a.xnorm)
-                    st4(a.xnorm + off, make_float4((v.x - p.x) * p.y, (v.y - p.x) * p.y, (v.z - p.x) * p.y,
-                                                   (v.w - p.x) * p.y));
-                st4(a.out + off, make_float4(bn_fwd1<A>(v.x, p.x, p.y, p.z, p.w, a.act),
-                                             bn_fwd1<A>(v.y, p.x, p.y, p.z, p.w, a.act),
-                                             bn_fwd1<A>(v.z, p.x, p.y, p.z, p.w, a.act),
-                                             bn_fwd1<A>(v.w, p.x, p.y, p.z, p.w, a.act)));
-            }
-        } else {
-            const float4 *bx = reinterpret_cast<const float4 *>(tensor_buf(a, s, stage, 1));
-            const float4 *by = reinterpret_cast<const float4 *>(tensor_buf(a, s, stage, NT - 1));
-            for (uint32_t i = threadIdx.x; i < n4; i += kPThreads) {
-                uint32_t u, r;
-                a.f_u4.divmod(i, u, r);
-                const UnitEntry e = ut[u];
-                const BwdParam p = *reinterpret_cast<const BwdParam *>(s.ptab + e.j * 8);
-                const float4 d = b0[i], xv = bx[i];
-                const float4 yv = HASY ? by[i] : xv;
-                const int64_t off = e.goff + 4 * (int64_t)r;
-                st4(a.out + off, make_float4(bn_dx_p(bn_grad1<A, HASY>(d.x, xv.x, yv.x, p, a.act), xv.x, p, a),
-                                             bn_dx_p(bn_grad1<A, HASY>(d.y, xv.y, yv.y, p, a.act), xv.y, p, a),
-                                             bn_dx_p(bn_grad1<A, HASY>(d.z, xv.z, yv.z, p, a.act), xv.z, p, a),
-                                             bn_dx_p(bn_grad1<A, HASY>(d.w, xv.w, yv.w, p, a.act), xv.w, p, a)));
-            }
-        }
+        return make_float4(c, m, q, 0.0f);
     }
 };
 
 #ifdef DNB_PHASE_TIMING
 // Diagnostic build only (-DDNB_PHASE_TIMING): %globaltimer stamps per (CTA, group, phase):
-// 0 copies landed, 1 partials published, 2 group barrier released, 3 merge done, 4 apply done.
-constexpr int kTsCtas = 160, kTsGroups = 64, kTsPhases = 6;
+// stats role 0 start, 1 published; apply role 2 released, 3 merged, 4 applied.
+constexpr int kTsCtas = 1280, kTsGroups = 32, kTsPhases = 6;
 __device__ unsigned long long g_phase_ts[kTsCtas * kTsGroups * kTsPhases];
 #define DNB_STAMP(g, ph)                                                                              \
     do {                                                                                              \
@@ -852,157 +601,551 @@ __device__ unsigned long long g_phase_ts[kTsCtas * kTsGroups * kTsPhases];
     } while (0)
 #endif
 
-// Software pipeline, `stages` groups deep. Iteration g:
-//   wait for group g+1's copies; reduce them; publish (arrive on g+1)
-//   wait for group g's arrivals (published one iteration earlier, so normally complete)
-//   merge group g's records; write group g's outputs from shared memory
-//   refill the freed stage with group g+stages
-// The copy of a group is issued `stages - 1` iterations before it is reduced, and the
-// grid-wide wait for a group trails its arrivals by one iteration of work.
 template <bool BWD, int A, bool HASY>
-__global__ void __launch_bounds__(kPThreads, kPMinBlocks) k_bn_persistent(PArgs a) {
-    using K = PKernel<BWD, A, HASY>;
+struct PipeKernel {
+    static constexpr int NT = BWD ? (HASY ? 3 : 2) : 1;  // tensors staged per unit
+
+    struct Smem {
+        float *buf;        // [2][NT][cap_units * U]
+        long long *utab;   // [2][cap_units] element offset of each staged unit
+        uint64_t *bars;    // [2]
+        float4 *wrec;      // [2 segments][kLWarps] warp partials of the stats role
+        float *ptab;       // [2 segments][8] apply records of the current group
+        int *flag;
+    };
+    __host__ __device__ static size_t buf_bytes(int cap_units, int U) {
+        return (size_t)2 * NT * cap_units * U * sizeof(float);
+    }
+    __host__ __device__ static size_t smem_bytes(int cap_units, int U) {
+        return buf_bytes(cap_units, U) + (size_t)2 * cap_units * sizeof(long long) + 2 * sizeof(uint64_t) +
+               2 * kLWarps * sizeof(float4) + 16 * sizeof(float) + 16;
+    }
+    __device__ static Smem carve(const PArgs &a, unsigned char *raw) {
+        Smem s;
+        size_t o = buf_bytes(a.cap_units, a.U);
+        s.buf = reinterpret_cast<float *>(raw);
+        s.utab = reinterpret_cast<long long *>(raw + o);
+        o += (size_t)2 * a.cap_units * sizeof(long long);
+        s.bars = reinterpret_cast<uint64_t *>(raw + o);
+        o += 2 * sizeof(uint64_t);
+        s.wrec = reinterpret_cast<float4 *>(raw + o);
+        o += 2 * kLWarps * sizeof(float4);
+        s.ptab = reinterpret_cast<float *>(raw + o);
+        o += 16 * sizeof(float);
+        s.flag = reinterpret_cast<int *>(raw + o);
+        return s;
+    }
+    __device__ static float *tbuf(const PArgs &a, const Smem &s, int b, int t) {
+        return s.buf + ((size_t)b * NT + t) * a.cap_units * a.U;
+    }
+
+    // Copies of the share (role partition `parts`) of group g into buffer b (warp 0).
+    __device__ static void issue(const PArgs &a, const Smem &s, int g, int rid, const FastDiv &parts, int b) {
+        if (threadIdx.x >= 32) return;
+        const Share sh = share_of(a, g, rid, parts);
+        const int n_units = (int)(sh.t1 - sh.t0);
+        const unsigned unit_bytes = (unsigned)a.U * sizeof(float);
+        if (threadIdx.x == 0) {
+            fence_proxy_async();  // this buffer's earlier generic-proxy reads come first
+            mbar_arrive_expect_tx(&s.bars[b], (unsigned)(n_units * NT) * unit_bytes);
+        }
+        __syncwarp();
+        const float *src[3] = {a.t0, a.t1, a.t2};
+        for (int u = threadIdx.x; u < n_units; u += 32) {
+            uint32_t cl, rem, n, k;
+            a.f_nk.divmod(sh.t0 + u, cl, rem);
+            a.f_k.divmod(rem, n, k);
+            const int64_t goff = ((int64_t)n * a.C + sh.c0 + cl) * a.S + (int64_t)k * a.U;
+            s.utab[b * a.cap_units + u] = goff;
+#pragma unroll
+            for (int tt = 0; tt < NT; ++tt)
+                bulk_g2s(tbuf(a, s, b, tt) + (size_t)u * a.U, src[tt] + goff, unit_bytes, &s.bars[b]);
+        }
+    }
+
+    // Bounded wait for buffer b's copies (phase parity); every thread calls it.
+    __device__ static bool wait_copies(const PArgs &a, const Smem &s, int b, unsigned parity) {
+        const unsigned long long deadline = global_ns() + a.wait_ns;
+        unsigned it = 0;
+        while (!mbar_try_wait(&s.bars[b], parity)) {
+            if ((++it & 63u) == 0 && global_ns() > deadline) {
+                atomicOr(a.err, DEVERR_WAIT_COPY);
+                atomicExch(a.abort_flag, 1u);
+                return false;
+            }
+        }
+        return true;
+    }
+
+    __device__ static BwdParam fwd_params_of(const PArgs &a, int64_t c) {
+        BwdParam p;
+        p.m = a.mean_in[c];
+        p.inv = 1.0f / (sqrtf(a.var_in[c]) + 0.000001f);
+        p.g = a.scales[c];
+        p.b = a.biases[c];
+        return p;
+    }
+
+    // stats role: records of CTA `rid`'s share of group g, staged in buffer b
+    __device__ static void stats(const PArgs &a, const Smem &s, int g, int rid, int b) {
+        const Share sh = share_of(a, g, rid, a.f_ps);
+        if (sh.nseg == 0) return;
+        const uint32_t u4 = (uint32_t)a.U >> 2;
+        const uint32_t n4 = (sh.t1 - sh.t0) * u4;
+        const uint32_t i_bnd = ((sh.t1 < sh.bnd ? sh.t1 : sh.bnd) - sh.t0) * u4;  // first float4 of segment 1
+        const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+        const float4 *b0 = reinterpret_cast<const float4 *>(tbuf(a, s, b, 0));
+        float4 rec[2];
+        if constexpr (!BWD) {
+            Moments mo[2];
+#pragma unroll 4
+            for (uint32_t i = threadIdx.x; i < n4; i += kLThreads) {
+                const float4 v = b0[i];
+                if (i < i_bnd) mo[0].add4(v);
+                else mo[1].add4(v);
+            }
+            rec[0] = mo[0].warp_summary();
+            rec[1] = mo[1].warp_summary();
+        } else {
+            const float4 *bx = reinterpret_cast<const float4 *>(tbuf(a, s, b, 1));
+            const float4 *by = reinterpret_cast<const float4 *>(tbuf(a, s, b, NT - 1));
+            const BwdParam p0 = fwd_params_of(a, (int64_t)sh.c0 + sh.cfirst);
+            const BwdParam p1 = sh.nseg > 1 ? fwd_params_of(a, (int64_t)sh.c0 + sh.cfirst + 1) : p0;
+            float s1[2] = {0.0f, 0.0f}, s2[2] = {0.0f, 0.0f};
+#pragma unroll 2
+            for (uint32_t i = threadIdx.x; i < n4; i += kLThreads) {
+                const int sg = i < i_bnd ? 0 : 1;
+                const BwdParam &p = sg ? p1 : p0;
+                const float4 d = b0[i], xv = bx[i];
+                const float4 yy = HASY ? by[i] : xv;
+                const float g0 = bn_grad1<A, HASY>(d.x, xv.x, yy.x, p, a.act);
+                const float g1 = bn_grad1<A, HASY>(d.y, xv.y, yy.y, p, a.act);
+                const float g2 = bn_grad1<A, HASY>(d.z, xv.z, yy.z, p, a.act);
+                const float g3 = bn_grad1<A, HASY>(d.w, xv.w, yy.w, p, a.act);
+                const float t1 = (g0 + g1) + (g2 + g3);
+                const float t2 = (g0 * (xv.x - p.m) + g1 * (xv.y - p.m)) + (g2 * (xv.z - p.m) + g3 * (xv.w - p.m));
+                if (sg) {
+                    s1[1] += t1;
+                    s2[1] += t2;
+                } else {
+                    s1[0] += t1;
+                    s2[0] += t2;
+                }
+            }
+            rec[0] = make_float4(warp_sum(s1[0]), warp_sum(s2[0]), 0.0f, 0.0f);
+            rec[1] = make_float4(warp_sum(s1[1]), warp_sum(s2[1]), 0.0f, 0.0f);
+        }
+        // one record per (CTA, segment): warp 0 combines the warps' partials
+        if (lane == 0) {
+            s.wrec[warp] = rec[0];
+            s.wrec[kLWarps + warp] = rec[1];
+        }
+        __syncthreads();
+        if (warp == 0) {
+            for (int j = 0; j < sh.nseg; ++j) {
+                float4 r = lane < kLWarps ? s.wrec[j * kLWarps + lane] : make_float4(0, 0, 0, 0);
+                if constexpr (!BWD) {
+#pragma unroll
+                    for (int o = kLWarps / 2; o > 0; o >>= 1) {
+                        const float cb = __shfl_xor_sync(0xffffffffu, r.x, o);
+                        const float mb = __shfl_xor_sync(0xffffffffu, r.y, o);
+                        const float qb = __shfl_xor_sync(0xffffffffu, r.z, o);
+                        chan_merge(r.x, r.y, r.z, cb, mb, qb);
+                    }
+                } else {
+#pragma unroll
+                    for (int o = kLWarps / 2; o > 0; o >>= 1) {
+                        r.x += __shfl_xor_sync(0xffffffffu, r.x, o);
+                        r.y += __shfl_xor_sync(0xffffffffu, r.y, o);
+                    }
+                }
+                if (lane == 0) a.rec[((int64_t)g * a.Ps + rid) * 2 + j] = r;
+            }
+        }
+    }
+
+    // One release-add per CTA on counter[g] after the whole CTA's work (CTA barrier, then
+    // a GPU-scope fence by thread 0, as a grid barrier publishes a CTA's writes).
+    __device__ static void arrive(unsigned *counter, int g) {
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            __threadfence();
+            asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(counter + g) : "memory");
+        }
+    }
+
+    // Wait (bounded) until counter[g] reaches `target`; block-uniform result.
+    __device__ static bool wait_for(const PArgs &a, int *flag, const unsigned *counter, int g, unsigned target) {
+        if (threadIdx.x == 0) {
+            int ok = 1;
+            if (ld_acquire_gpu(&counter[g]) < target) {
+                const unsigned long long deadline = global_ns() + a.wait_ns;
+                while (ld_acquire_gpu(&counter[g]) < target) {
+                    if (ld_volatile(a.abort_flag)) {
+                        ok = 0;
+                        break;
+                    }
+                    if (global_ns() > deadline) {
+                        atomicOr(a.err, DEVERR_WAIT_BARRIER);
+                        atomicExch(a.abort_flag, 1u);
+                        ok = 0;
+                        break;
+                    }
+                    __nanosleep(64);
+                }
+            }
+            *flag = ok;
+        }
+        __syncthreads();
+        return *flag != 0;
+    }
+
+    // Non-blocking: has counter[g] reached `target`? Block-uniform.
+    __device__ static bool ready(int *flag, const unsigned *counter, int g, unsigned target) {
+        if (threadIdx.x == 0) *flag = ld_acquire_gpu(&counter[g]) >= target;
+        __syncthreads();
+        return *flag != 0;
+    }
+
+    // apply role: merge the records of the (at most two) channels of CTA `rid`'s share.
+    // Records of stats CTAs between the first and last owner that hold no unit of the
+    // channel (a group with fewer units than CTAs) are skipped.
+    __device__ static void merge(const PArgs &a, float *ptab, int g, int rid) {
+        const Share sh = share_of(a, g, rid, a.f_pa);
+        const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+        if (warp < sh.nseg) {
+            const int cl = sh.cfirst + warp;
+            const int64_t c = (int64_t)sh.c0 + cl;
+            // per-channel inputs are requested before the records so the loads overlap
+            float gamma = 0.0f, beta = 0.0f, m_in = 0.0f, v_in = 0.0f, rm = 0.0f, rv = 0.0f;
+            const uint32_t ua = (uint32_t)cl * a.NK, ub = ua + a.NK;
+            // the apply CTA owning the channel's first unit writes the per-channel outputs
+            const bool write = owner_of(a, g, ua, a.Pa) == rid;
+            if (lane == 0) {
+                gamma = a.scales[c];
+                beta = a.biases[c];
+                if constexpr (BWD) {
+                    m_in = a.mean_in[c];
+                    v_in = a.var_in[c];
+                } else if (write) {
+                    rm = a.rmean[c];
+                    rv = a.rvar[c];
+                }
+            }
+            const int plo = owner_of(a, g, ua, a.Ps), phi = owner_of(a, g, ub - 1, a.Ps);
+            const int nrec = phi - plo + 1;
+            float *out = ptab + warp * 8;
+            constexpr int R = 2;  // records held per lane: one L2 round trip up to 64 records
+            float4 r[R];
+            bool have[R];
+            auto load = [&](int idx, float4 &dst) -> bool {
+                const int p = plo + idx;
+                const Share o = share_of(a, g, p, a.f_ps);
+                const uint32_t lo = ua > o.t0 ? ua : o.t0, hi = ub < o.t1 ? ub : o.t1;
+                if (hi <= lo) return false;
+                dst = __ldcg(&a.rec[((int64_t)g * a.Ps + p) * 2 + (cl - o.cfirst)]);
+                return true;
+            };
+#pragma unroll
+            for (int k = 0; k < R; ++k) {
+                const int idx = lane + 32 * k;
+                have[k] = idx < nrec && load(idx, r[k]);
+            }
+            if constexpr (!BWD) {
+                double sn = 0.0, smn = 0.0;
+#pragma unroll
+                for (int k = 0; k < R; ++k)
+                    if (have[k]) {
+                        sn += (double)r[k].x;
+                        smn += (double)r[k].x * (double)r[k].y;
+                    }
+                for (int idx = lane + 32 * R; idx < nrec; idx += 32) {
+                    float4 t;
+                    if (!load(idx, t)) continue;
+                    sn += (double)t.x;
+                    smn += (double)t.x * (double)t.y;
+                }
+                sn = warp_sum(sn);
+                const double mu = warp_sum(smn) / sn;
+                double m2 = 0.0;
+#pragma unroll
+                for (int k = 0; k < R; ++k)
+                    if (have[k]) {
+                        const double d = (double)r[k].y - mu;
+                        m2 += (double)r[k].z + (double)r[k].x * d * d;
+                    }
+                for (int idx = lane + 32 * R; idx < nrec; idx += 32) {
+                    float4 t;
+                    if (!load(idx, t)) continue;
+                    const double d = (double)t.y - mu;
+                    m2 += (double)t.z + (double)t.x * d * d;
+                }
+                m2 = warp_sum(m2);
+                if (lane == 0) {
+                    const FwdClose f = fwd_close(mu, m2, sn);
+                    if (write) {
+                        a.mean[c] = f.m;
+                        a.var[c] = f.var;
+                        a.rmean[c] = rolling(rm, f.m);
+                        a.rvar[c] = rolling(rv, f.var);
+                    }
+                    out[0] = f.m;
+                    out[1] = f.inv;
+                    out[2] = gamma;
+                    out[3] = beta;
+                }
+            } else {
+                double s1 = 0.0, s2 = 0.0;
+#pragma unroll
+                for (int k = 0; k < R; ++k)
+                    if (have[k]) {
+                        s1 += (double)r[k].x;
+                        s2 += (double)r[k].y;
+                    }
+                for (int idx = lane + 32 * R; idx < nrec; idx += 32) {
+                    float4 t;
+                    if (!load(idx, t)) continue;
+                    s1 += (double)t.x;
+                    s2 += (double)t.y;
+                }
+                s1 = warp_sum(s1);
+                s2 = warp_sum(s2);
+                if (lane == 0) {
+                    const BwdParam bp = bwd_close(s1, s2, m_in, v_in, gamma, beta, a.denom, a.bias_upd, a.scale_upd,
+                                                  a.mean_delta, a.var_delta, c, write);
+                    *reinterpret_cast<BwdParam *>(out) = bp;
+                }
+            }
+        }
+        __syncthreads();
+    }
+
+    // apply role: outputs of CTA `rid`'s share of group g from buffer b. Thread i walks the
+    // share's float4s i, i + kLThreads, ... tracking (unit, float4 within unit) by
+    // increments; a unit's element offset comes from the table written at copy time.
+    __device__ static void apply(const PArgs &a, const Smem &s, int g, int rid, int b) {
+        const Share sh = share_of(a, g, rid, a.f_pa);
+        if (sh.nseg == 0) return;
+        const uint32_t u4 = (uint32_t)a.U >> 2;
+        const uint32_t n4 = (sh.t1 - sh.t0) * u4;
+        const uint32_t i_bnd = ((sh.t1 < sh.bnd ? sh.t1 : sh.bnd) - sh.t0) * u4;
+        const long long *ut = s.utab + b * a.cap_units;
+        const float4 *b0 = reinterpret_cast<const float4 *>(tbuf(a, s, b, 0));
+        uint32_t u, r;
+        a.f_u4.divmod(threadIdx.x, u, r);
+        if constexpr (!BWD) {
+            const float4 q0 = *reinterpret_cast<const float4 *>(s.ptab);
+            const float4 q1 = *reinterpret_cast<const float4 *>(s.ptab + 8);
+#pragma unroll 4
+            for (uint32_t i = threadIdx.x; i < n4; i += kLThreads) {
+                const int64_t off = ut[u] + 4 * (int64_t)r;
+                const float4 v = b0[i];
+                const float4 p = i < i_bnd ? q0 : q1;
+                if (a.xnorm)
+                    st4_stream(a.xnorm + off, make_float4((v.x - p.x) * p.y, (v.y - p.x) * p.y, (v.z - p.x) * p.y,
+                                                          (v.w - p.x) * p.y));
+                st4_stream(a.out + off, make_float4(bn_fwd1<A>(v.x, p.x, p.y, p.z, p.w, a.act),
+                                                    bn_fwd1<A>(v.y, p.x, p.y, p.z, p.w, a.act),
+                                                    bn_fwd1<A>(v.z, p.x, p.y, p.z, p.w, a.act),
+                                                    bn_fwd1<A>(v.w, p.x, p.y, p.z, p.w, a.act)));
+                u += a.step_q;
+                r += a.step_r;
+                if (r >= u4) {
+                    r -= u4;
+                    ++u;
+                }
+            }
+        } else {
+            const float4 *bx = reinterpret_cast<const float4 *>(tbuf(a, s, b, 1));
+            const float4 *by = reinterpret_cast<const float4 *>(tbuf(a, s, b, NT - 1));
+            const BwdParam q0 = *reinterpret_cast<const BwdParam *>(s.ptab);
+            const BwdParam q1 = *reinterpret_cast<const BwdParam *>(s.ptab + 8);
+#pragma unroll 2
+            for (uint32_t i = threadIdx.x; i < n4; i += kLThreads) {
+                const int64_t off = ut[u] + 4 * (int64_t)r;
+                const BwdParam &p = i < i_bnd ? q0 : q1;
+                const float4 d = b0[i], xv = bx[i];
+                const float4 yy = HASY ? by[i] : xv;
+                st4_stream(a.out + off,
+                           make_float4(bn_dx_p(bn_grad1<A, HASY>(d.x, xv.x, yy.x, p, a.act), xv.x, p, a),
+                                       bn_dx_p(bn_grad1<A, HASY>(d.y, xv.y, yy.y, p, a.act), xv.y, p, a),
+                                       bn_dx_p(bn_grad1<A, HASY>(d.z, xv.z, yy.z, p, a.act), xv.z, p, a),
+                                       bn_dx_p(bn_grad1<A, HASY>(d.w, xv.w, yy.w, p, a.act), xv.w, p, a)));
+                u += a.step_q;
+                r += a.step_r;
+                if (r >= u4) {
+                    r -= u4;
+                    ++u;
+                }
+            }
+        }
+    }
+};
+
+template <bool BWD, int A, bool HASY>
+__global__ void __launch_bounds__(kLThreads, 2) k_bn_persistent(PArgs a) {
+    using K = PipeKernel<BWD, A, HASY>;
     extern __shared__ __align__(128) unsigned char smem_raw[];
     const typename K::Smem s = K::carve(a, smem_raw);
     __shared__ unsigned s_epoch;
 
     if (threadIdx.x == 0) {
         s_epoch = ld_volatile(&a.sync[0]);
-        for (int i = 0; i < a.stages; ++i) mbar_init(&s.bars[i], 1);
+        mbar_init(&s.bars[0], 1);
+        mbar_init(&s.bars[1], 1);
         fence_mbar_init();
     }
     __syncthreads();
     const unsigned epoch = s_epoch;
-    unsigned *cnt = a.sync + 1 + (epoch & 1u) * kMaxGroups;
-    if (blockIdx.x == 0) {
-        unsigned *other = a.sync + 1 + ((epoch & 1u) ^ 1u) * kMaxGroups;
-        for (int i = threadIdx.x; i < kMaxGroups; i += kPThreads) other[i] = 0u;
-    }
+    unsigned *stats_done = a.sync + 1 + (size_t)(epoch & 1u) * 2 * kMaxGroups;
+    unsigned *apply_done = stats_done + kMaxGroups;
+    const bool stats_role = (blockIdx.x & 1u) == 0;
+    const int rid = (int)(blockIdx.x >> 1);
+    // pending[b] = parity of the copy outstanding on buffer b, or -1
+    int pending[2] = {-1, -1};
+    unsigned uses[2] = {0, 0};
+    auto issue = [&](int g, const FastDiv &parts, int b) {
+        K::issue(a, s, g, rid, parts, b);
+        pending[b] = (int)(uses[b] & 1u);
+        ++uses[b];
+    };
+    bool ok = true;
 
-    // pending[st] = parity of the copy outstanding on stage st, or -1
-    int pending[kMaxStages] = {-1, -1, -1};
-    unsigned uses[kMaxStages] = {0, 0, 0};
-
-    const int pre = a.G < a.stages ? a.G : a.stages;
-    for (int g = 0; g < pre; ++g) {
-        K::issue(a, s, g, g);
-        pending[g] = (int)(uses[g] & 1u);
-        ++uses[g];
-    }
-    // every wait result is made block-uniform before it steers control flow, so no thread
-    // can leave the loop while others continue into a barrier
-    bool ok = __syncthreads_and(K::wait_copies(a, s, 0, (unsigned)pending[0])) != 0;
-    DNB_STAMP(0, 0);
-    if (ok) {
-        K::stats(a, s, 0, 0);
-        K::arrive(a, cnt, 0, a.G == 1, epoch);
-        DNB_STAMP(0, 1);
-    }
-    for (int g = 0; ok && g < a.G; ++g) {
-        const int st = g % a.stages;
-        if (g + 1 < a.G) {
-            const int st1 = (g + 1) % a.stages;
-            ok = __syncthreads_and(K::wait_copies(a, s, st1, (unsigned)pending[st1])) != 0;
-            DNB_STAMP(g + 1, 0);
-            if (!ok) break;
-            K::stats(a, s, g + 1, st1);
-            K::arrive(a, cnt, g + 1, g + 2 == a.G, epoch);
-            DNB_STAMP(g + 1, 1);
+    if (stats_role) {
+        if (rid == 0) {  // the next launch's bank
+            unsigned *other = a.sync + 1 + (size_t)((epoch & 1u) ^ 1u) * 2 * kMaxGroups;
+            for (int i = threadIdx.x; i < 2 * kMaxGroups; i += kLThreads) other[i] = 0u;
         }
-        ok = K::wait_group(a, s, cnt, g);
-        DNB_STAMP(g, 2);
-        if (!ok) break;
-        K::finalize(a, s, g);
-        DNB_STAMP(g, 3);
-        K::apply(a, s, g, st);
-        pending[st] = -1;
-        __syncthreads();  // every thread is done reading stage st
-        DNB_STAMP(g, 4);
-        if (g + a.stages < a.G) {
-            K::issue(a, s, g + a.stages, st);
-            pending[st] = (int)(uses[st] & 1u);
-            ++uses[st];
+        issue(0, a.f_ps, 0);
+        if (a.G > 1) issue(1, a.f_ps, 1);
+        for (int g = 0; g < a.G; ++g) {
+            const int b = g & 1;
+            // every wait result is made block-uniform before it steers control flow
+            ok = __syncthreads_and(K::wait_copies(a, s, b, (unsigned)pending[b])) != 0;
+            if (!ok) break;
+            DNB_STAMP(g, 0);
+            K::stats(a, s, g, rid, b);
+            pending[b] = -1;
+            K::arrive(stats_done, g);  // its barrier also ends every read of buffer b
+            DNB_STAMP(g, 1);
+            const int h = g + 2;
+            if (h < a.G) {
+                if (h >= a.depth && !K::wait_for(a, s.flag, apply_done, h - a.depth, (unsigned)a.Pa)) {
+                    ok = false;
+                    break;
+                }
+                issue(h, a.f_ps, b);
+            }
+        }
+        // every CTA has read the epoch once every apply CTA has counted itself in the last
+        // group: advance it for the next launch
+        if (rid == 0 && ok && K::wait_for(a, s.flag, apply_done, a.G - 1, (unsigned)a.Pa) && threadIdx.x == 0)
+            atomicExch(&a.sync[0], epoch + 1);
+    } else {
+        bool next_issued = false;
+        ok = K::wait_for(a, s.flag, stats_done, 0, (unsigned)a.Ps);
+        if (ok) issue(0, a.f_pa, 0);
+        for (int g = 0; ok && g < a.G; ++g) {
+            const int b = g & 1;
+            // start the copy of group g+1 now if its stats are already complete
+            next_issued = false;
+            if (g + 1 < a.G && K::ready(s.flag, stats_done, g + 1, (unsigned)a.Ps)) {
+                issue(g + 1, a.f_pa, b ^ 1);
+                next_issued = true;
+            }
+            DNB_STAMP(g, 2);
+            K::merge(a, s.ptab, g, rid);
+            DNB_STAMP(g, 3);
+            ok = __syncthreads_and(K::wait_copies(a, s, b, (unsigned)pending[b])) != 0;
+            if (!ok) break;
+            K::apply(a, s, g, rid, b);
+            pending[b] = -1;
+            K::arrive(apply_done, g);
+            DNB_STAMP(g, 4);
+            if (g + 1 < a.G && !next_issued) {
+                ok = K::wait_for(a, s.flag, stats_done, g + 1, (unsigned)a.Ps);
+                if (!ok) break;
+                issue(g + 1, a.f_pa, b ^ 1);
+            }
         }
     }
     if (!ok) {
         // leave no copy in flight into this CTA's shared memory
-        for (int st = 0; st < a.stages; ++st)
-            if (pending[st] >= 0) K::wait_copies(a, s, st, (unsigned)pending[st]);
+        for (int b = 0; b < 2; ++b)
+            if (pending[b] >= 0) K::wait_copies(a, s, b, (unsigned)pending[b]);
     }
 }
 
 struct PPlan {
     bool ok = false;
-    int K, U, cap_units, cg, G, P, maxj, stages, ctas_per_sm;
+    int K, U, cg, G, P, depth, cap_units, ctas_per_sm;
     size_t smem;
 };
 
-// Shapes the persistent kernel: units of U = spatial/K floats (U % 4 == 0), a stage
-// buffer per tensor of cap_units units, cg channels per group.
+int env_int(const char *name, int dflt, int lo, int hi) {
+    const char *e = getenv(name);
+    int v = e ? atoi(e) : dflt;
+    return v < lo ? lo : (v > hi ? hi : v);
+}
+
+// One CTA of each role per SM by default (DNB_BN_CTAS_PER_SM, even); each CTA double-buffers
+// its share of a group in shared memory, so a group holds at most
+// cap_units * (CTAs per role) units; DNB_BN_GROUP_MB (default: as large as that allows)
+// can make groups smaller. Units are U = spatial/K floats, K the smallest divisor for which
+// a unit fits a buffer and every CTA gets >= 4 units; cg stays <= CTAs per role so a share
+// spans at most two channels.
 template <bool BWD, bool HASY>
-PPlan plan_persistent(int64_t batch, int64_t filters, int64_t spatial, const DeviceState *ds, int stages) {
-    using K = PKernel<BWD, DNB_ACT_LEAKY, HASY>;
+PPlan plan_persistent(int64_t batch, int64_t filters, int64_t spatial, const DeviceState *ds, int occupancy) {
+    using K = PipeKernel<BWD, DNB_ACT_LEAKY, HASY>;
+    constexpr int nt = K::NT;
     PPlan pl;
     if (spatial % 4 != 0 || batch <= 0 || filters <= 0) return pl;
-    const int nt = K::NT;
-    // CTAs per SM: two by default, so one CTA's barrier wait and merge overlap the other's
-    // reduction and writes
-    const char *env_c = getenv("DNB_BN_CTAS_PER_SM");
-    int ctas = env_c ? atoi(env_c) : 2;
-    if (ctas < 1) ctas = 1;
-    if (ctas > 4) ctas = 4;
+    int ctas = env_int("DNB_BN_CTAS_PER_SM", 2, 2, 8) & ~1;
+    if (ctas > occupancy) ctas = occupancy & ~1;
+    if (ctas < 2) return pl;
     size_t per_cta = (size_t)ds->smem_per_sm / ctas - (size_t)ds->smem_reserved - 256;  // 256: static smem
     if (per_cta > (size_t)ds->max_smem_optin) per_cta = (size_t)ds->max_smem_optin;
-    const size_t budget = per_cta - 4096;  // unit tables, apply records, reduction scratch, barriers
-    const size_t per_tensor = budget / ((size_t)stages * nt);
-    // smallest K dividing spatial with U % 4 == 0 and one unit fitting a stage buffer
-    int64_t k = 1;
-    for (; k <= spatial; ++k) {
-        if (spatial % k) continue;
-        const int64_t u = spatial / k;
-        if (u % 4 == 0 && (size_t)u * 4 <= per_tensor) break;
+    const size_t per_buf = (per_cta - 512) / (2 * nt);  // one buffer, one tensor
+    const int64_t P = (int64_t)ds->sm_count * ctas, half = P / 2;
+    int64_t k = 0;
+    for (int64_t kk = 1; kk <= spatial; ++kk) {
+        if (spatial % kk || (spatial / kk) % 4 || (size_t)(spatial / kk) * 4 > per_buf) continue;
+        if (k == 0) k = kk;
+        if (filters * batch * kk >= 4 * half || spatial / kk <= 64) {
+            k = kk;
+            break;
+        }
     }
-    if (k > spatial) return pl;
+    if (k == 0) return pl;
     const int64_t U = spatial / k, NK = batch * k;
-    int64_t cap = (int64_t)(per_tensor / ((size_t)U * 4));
-    const int64_t P = (int64_t)ds->sm_count * ctas;
-    int64_t cg_max = cap * P / NK;
-    if (cg_max < 1) return pl;
-    // at least ~6 groups so the copy of the next group overlaps the current one
-    const char *env = getenv("DNB_BN_MIN_GROUPS");
-    const int64_t min_groups = env ? atoll(env) : 6;
-    int64_t cg = cg_max;
-    if (min_groups > 1) {
-        const int64_t want = (filters + min_groups - 1) / min_groups;
-        if (want < cg) cg = want < 1 ? 1 : want;
+    const int64_t cap = (int64_t)(per_buf / ((size_t)U * 4));
+    int64_t cg = cap * half / NK;
+    const int group_mb = env_int("DNB_BN_GROUP_MB", 0, 0, 4096);
+    if (group_mb > 0) {
+        const int64_t want = ((int64_t)group_mb << 20) / (batch * spatial * 4 * nt);
+        if (want < cg) cg = want;
     }
+    if (cg > half) cg = half;
+    if (cg > filters) cg = filters;
+    if (cg < 1) return pl;
     int64_t G = (filters + cg - 1) / cg;
     cg = (filters + G - 1) / G;
     G = (filters + cg - 1) / cg;
     if (G > kMaxGroups) return pl;
-    const int64_t share = (cg * NK + P - 1) / P;
-    if (share > cap) return pl;
-    // 32-bit partition arithmetic: every product is at most T*P <= share*P*P
-    if ((uint64_t)share * P * P >= (1ull << 32)) return pl;
-    cap = share;  // stage buffers only as large as a share
+    const int64_t T = cg * NK;
+    const int64_t share = (T + half - 1) / half;
+    if (share > cap || (uint64_t)T * (uint64_t)half >= (1ull << 32) - (uint64_t)half) return pl;
     pl.K = (int)k;
     pl.U = (int)U;
-    pl.cap_units = (int)cap;
     pl.cg = (int)cg;
     pl.G = (int)G;
     pl.P = (int)P;
-    pl.maxj = (int)((cap - 1) / NK + 2);
-    pl.stages = stages;
-    pl.smem = K::smem_bytes(stages, pl.cap_units, pl.U, pl.maxj);
-    pl.ok = pl.smem <= per_cta;
+    pl.depth = env_int("DNB_BN_DEPTH", 4, 3, 16);
+    pl.cap_units = (int)share;  // buffers only as large as a share
     pl.ctas_per_sm = ctas;
+    pl.smem = K::smem_bytes(pl.cap_units, pl.U);
+    pl.ok = pl.smem <= per_cta;
     return pl;
-}
-
-int stages_from_env() {
-    const char *e = getenv("DNB_BN_STAGES");
-    int s = e ? atoi(e) : 3;
-    return s < 2 ? 2 : (s > kMaxStages ? kMaxStages : s);
 }
 
 bool persistent_disabled() {
@@ -1010,65 +1153,84 @@ bool persistent_disabled() {
     return e && e[0] == '0';
 }
 
+// Plans and launches the persistent kernel for `a` (tensor and parameter pointers already
+// set). *launched stays false when the shape is not one the kernel takes.
 template <bool BWD, bool HASY>
-dnb_status launch_persistent(const PPlan &pl, PArgs &a, int act, cudaStream_t stream, const char *what) {
-    return dispatch_act(act, [&]<int A>() -> dnb_status {
-        auto kern = k_bn_persistent<BWD, A, HASY>;
-        DNB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem));
-        int per_sm = 0;
-        DNB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kPThreads, pl.smem));
-        if (per_sm < pl.ctas_per_sm)
-            return fail(DNB_ERR_UNSUPPORTED, "%s: %d CTAs of the persistent kernel fit an SM, the plan needs %d",
-                        what, per_sm, pl.ctas_per_sm);
-        void *args[] = {&a};
-        DNB_CUDA(cudaLaunchCooperativeKernel((const void *)kern, dim3((unsigned)pl.P), dim3(kPThreads), args, pl.smem,
-                                             stream));
-        return after_launch(stream, what);
-    });
-}
-
-template <bool BWD, bool HASY>
-dnb_status prepare_persistent(int64_t batch, int64_t filters, int64_t spatial, cudaStream_t stream, PPlan *pl_out,
-                              PArgs *a) {
+dnb_status run_persistent(int64_t batch, int64_t filters, int64_t spatial, int act, PArgs a, cudaStream_t stream,
+                          bool *launched, const char *what) {
+    *launched = false;
     DeviceState *ds = nullptr;
     DNB_TRY(current_device(&ds));
-    const PPlan pl = plan_persistent<BWD, HASY>(batch, filters, spatial, ds, stages_from_env());
-    *pl_out = pl;
-    if (!pl.ok) return DNB_OK;
-    Workspace *ws = nullptr;
-    DNB_TRY(workspace(stream, sizeof(float2) * (size_t)pl.G * pl.P * pl.maxj, &ws));
-    a->C = filters;
-    a->S = spatial;
-    a->N = (int)batch;
-    a->K = pl.K;
-    a->U = pl.U;
-    a->NK = (int)(batch * pl.K);
-    a->cg = pl.cg;
-    a->G = pl.G;
-    a->P = pl.P;
-    a->cap_units = pl.cap_units;
-    a->maxj = pl.maxj;
-    a->stages = pl.stages;
-    a->f_u4 = FastDiv((uint32_t)(pl.U / 4));
-    a->f_nk = FastDiv((uint32_t)a->NK);
-    a->f_k = FastDiv((uint32_t)pl.K);
-    a->f_p = FastDiv((uint32_t)pl.P);
-    a->T_full = (uint32_t)pl.cg * (uint32_t)a->NK;
-    a->T_last = (uint32_t)(filters - (int64_t)(pl.G - 1) * pl.cg) * (uint32_t)a->NK;
-    a->f_tfull = FastDiv(a->T_full);
-    a->f_tlast = FastDiv(a->T_last);
-    a->denom = (float)(spatial * batch);
-    // dividing by a power of two equals multiplying by its exact reciprocal
-    int e2 = 0;
-    const float fr = frexpf(a->denom, &e2);
-    a->denom_pow2 = fr == 0.5f;
-    a->inv_denom = 1.0f / a->denom;
-    a->rec = static_cast<float2 *>(ws->scratch);
-    a->sync = ws->sync;
-    a->err = ds->error_word;
-    a->abort_flag = ds->abort_flag;
-    a->wait_ns = wait_limit_ns();
-    return DNB_OK;
+    return dispatch_act(act, [&]<int A>() -> dnb_status {
+        auto kern = k_bn_persistent<BWD, A, HASY>;
+        // CTAs of this instantiation one SM holds by registers and threads (shared memory
+        // is sized by the plan)
+        static int reg_occupancy = -1;
+        if (reg_occupancy < 0) {
+            cudaFuncAttributes fa;
+            DNB_CUDA(cudaFuncGetAttributes(&fa, kern));
+            const int regs = fa.numRegs > 0 ? fa.numRegs : 1;
+            reg_occupancy = 65536 / (regs * kLThreads);
+        }
+        const PPlan pl = plan_persistent<BWD, HASY>(batch, filters, spatial, ds, reg_occupancy);
+        if (!pl.ok) return DNB_OK;
+        static size_t smem_set = 0;
+        if (pl.smem > smem_set) {
+            DNB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem));
+            smem_set = pl.smem;
+        }
+        const int half = pl.P / 2;
+        Workspace *ws = nullptr;
+        DNB_TRY(workspace(stream, sizeof(float4) * (size_t)pl.G * half * 2, &ws));
+        a.C = filters;
+        a.S = spatial;
+        a.N = (int)batch;
+        a.K = pl.K;
+        a.U = pl.U;
+        a.NK = (int)(batch * pl.K);
+        a.cg = pl.cg;
+        a.G = pl.G;
+        a.Ps = half;
+        a.Pa = half;
+        a.depth = pl.depth;
+        a.cap_units = pl.cap_units;
+        a.T_full = (uint32_t)pl.cg * (uint32_t)a.NK;
+        a.T_last = (uint32_t)(filters - (int64_t)(pl.G - 1) * pl.cg) * (uint32_t)a.NK;
+        a.f_u4 = FastDiv((uint32_t)(pl.U / 4));
+        a.step_q = (uint32_t)(kLThreads / (pl.U / 4));
+        a.step_r = (uint32_t)(kLThreads % (pl.U / 4));
+        a.f_nk = FastDiv((uint32_t)a.NK);
+        a.f_k = FastDiv((uint32_t)pl.K);
+        a.f_ps = FastDiv((uint32_t)half);
+        a.f_pa = FastDiv((uint32_t)half);
+        a.f_tfull = FastDiv(a.T_full);
+        a.f_tlast = FastDiv(a.T_last);
+        a.denom = (float)(spatial * batch);
+        // dividing by a power of two equals multiplying by its exact reciprocal
+        int e2 = 0;
+        a.denom_pow2 = frexpf(a.denom, &e2) == 0.5f;
+        a.inv_denom = 1.0f / a.denom;
+        a.act = act;
+        a.rec = static_cast<float4 *>(ws->scratch);
+        a.sync = ws->sync;
+        a.err = ds->error_word;
+        a.abort_flag = ds->abort_flag;
+        a.wait_ns = wait_limit_ns();
+        // every CTA must be resident: a cooperative launch
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)pl.P);
+        cfg.blockDim = dim3(kLThreads);
+        cfg.dynamicSmemBytes = pl.smem;
+        cfg.stream = stream;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeCooperative;
+        attr[0].val.cooperative = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        DNB_CUDA(cudaLaunchKernelEx(&cfg, kern, a));
+        *launched = true;
+        return after_launch(stream, what);
+    });
 }
 
 }  // namespace
@@ -1099,22 +1261,19 @@ dnb_status dnb_bn_act_forward_train(const float *x, float *y, float *x_norm, int
     const cudaStream_t s = as_stream(stream);
     const bool al = aligned16(x) && aligned16(y) && (!x_norm || aligned16(x_norm));
     if (al && !persistent_disabled()) {
-        PPlan pl;
         PArgs a{};
-        DNB_TRY((prepare_persistent<false, false>(batch, filters, spatial, s, &pl, &a)));
-        if (pl.ok) {
-            a.t0 = x;
-            a.out = y;
-            a.xnorm = x_norm;
-            a.scales = scales;
-            a.biases = biases;
-            a.mean = mean;
-            a.var = variance;
-            a.rmean = rolling_mean;
-            a.rvar = rolling_variance;
-            a.act = act;
-            return launch_persistent<false, false>(pl, a, act, s, what);
-        }
+        a.t0 = x;
+        a.out = y;
+        a.xnorm = x_norm;
+        a.scales = scales;
+        a.biases = biases;
+        a.mean = mean;
+        a.var = variance;
+        a.rmean = rolling_mean;
+        a.rvar = rolling_variance;
+        bool launched = false;
+        DNB_TRY((run_persistent<false, false>(batch, filters, spatial, act, a, s, &launched, what)));
+        if (launched) return DNB_OK;
     }
     const GGeom g = make_ggeom(batch, filters, spatial, aligned16(x));
     Workspace *ws = nullptr;
@@ -1139,29 +1298,25 @@ dnb_status dnb_bn_act_backward(const float *x, const float *y, const float *delt
     const cudaStream_t s = as_stream(stream);
     const bool al = aligned16(x) && aligned16(delta) && aligned16(dx) && (!y || aligned16(y));
     if (al && !persistent_disabled()) {
-        PPlan pl;
         PArgs a{};
+        a.t0 = delta;
+        a.t1 = x;
+        a.t2 = y;
+        a.out = dx;
+        a.scales = scales;
+        a.biases = biases;
+        a.mean_in = mean;
+        a.var_in = variance;
+        a.bias_upd = bias_updates;
+        a.scale_upd = scale_updates;
+        a.mean_delta = mean_delta;
+        a.var_delta = variance_delta;
+        bool launched = false;
         if (y)
-            DNB_TRY((prepare_persistent<true, true>(batch, filters, spatial, s, &pl, &a)));
+            DNB_TRY((run_persistent<true, true>(batch, filters, spatial, act, a, s, &launched, what)));
         else
-            DNB_TRY((prepare_persistent<true, false>(batch, filters, spatial, s, &pl, &a)));
-        if (pl.ok) {
-            a.t0 = delta;
-            a.t1 = x;
-            a.t2 = y;
-            a.out = dx;
-            a.scales = scales;
-            a.biases = biases;
-            a.mean_in = mean;
-            a.var_in = variance;
-            a.bias_upd = bias_updates;
-            a.scale_upd = scale_updates;
-            a.mean_delta = mean_delta;
-            a.var_delta = variance_delta;
-            a.act = act;
-            return y ? launch_persistent<true, true>(pl, a, act, s, what)
-                     : launch_persistent<true, false>(pl, a, act, s, what);
-        }
+            DNB_TRY((run_persistent<true, false>(batch, filters, spatial, act, a, s, &launched, what)));
+        if (launched) return DNB_OK;
     }
     const GGeom g = make_ggeom(batch, filters, spatial, aligned16(x) && aligned16(delta) && (!y || aligned16(y)));
     Workspace *ws = nullptr;

@@ -60,7 +60,9 @@ struct Workspace {
     size_t scratch_bytes = 0;
 };
 
-constexpr int kMaxGroups = 2048;  // per bank; 1 + 2*kMaxGroups words of `sync`
+// `sync` = 1 epoch word + 2 banks, each holding two arrays of kMaxGroups group counters.
+constexpr int kMaxGroups = 1024;
+constexpr size_t kSyncWords = 1 + 4 * (size_t)kMaxGroups;
 
 // The state of the current device, initialising it on first use.
 dnb_status current_device(DeviceState **out);
@@ -114,6 +116,8 @@ struct FastDiv {
 
 __device__ __forceinline__ float4 ld4(const float *p) { return *reinterpret_cast<const float4 *>(p); }
 __device__ __forceinline__ void st4(float *p, float4 v) { *reinterpret_cast<float4 *>(p) = v; }
+// L2-only load (bypasses L1) for data another CTA will read again from L2.
+__device__ __forceinline__ float4 ld4_l2(const float *p) { return __ldcg(reinterpret_cast<const float4 *>(p)); }
 // Streaming (evict-first) variants for data touched exactly once.
 __device__ __forceinline__ float4 ld4_stream(const float *p) { return __ldcs(reinterpret_cast<const float4 *>(p)); }
 __device__ __forceinline__ void st4_stream(float *p, float4 v) { __stcs(reinterpret_cast<float4 *>(p), v); }

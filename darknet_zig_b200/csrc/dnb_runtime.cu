@@ -74,7 +74,7 @@ dnb_status workspace(cudaStream_t stream, size_t scratch_bytes, Workspace **out)
     Workspace *&ws = g_ws[{device, stream}];
     if (!ws) ws = new Workspace();
     ws->stream = stream;
-    const size_t want_sync = 1 + 2 * (size_t)kMaxGroups;
+    const size_t want_sync = kSyncWords;
     bool grow_sync = ws->sync_words < want_sync;
     bool grow_scratch = ws->scratch_bytes < scratch_bytes;
     if (grow_sync || grow_scratch) {
