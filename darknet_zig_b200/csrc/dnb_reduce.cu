@@ -212,3 +212,103 @@ dnb_status dnb_variance_delta(const float *x, const float *delta, const float *m
 }
 
 }  // extern "C"
+
+#include <mutex>
+
+// --------------------------------------------------------------------------------------
+// dnb_mean_noalloc: dnb_mean for callers that must not allocate device memory.
+//
+// Some hosts cannot call cudaMalloc on the path that computes batch statistics: code that
+// runs inside a pre-sized memory pool or arena (where every byte is budgeted up front),
+// code between the creation and the replay of a fixed memory plan, or a foreign runtime
+// that owns the device allocator. dnb_mean itself may grow the library's per-stream
+// workspace on first use; this variant keeps its per-(channel, chunk) partial sums in a
+// fixed array compiled into the library instead, and otherwise runs the same two kernels.
+//
+// The array is a file-scope __device__ object: every GPU that loads the library holds it
+// (kNoAllocScratchFloats floats, 1 MiB) until the process exits. Host code may not pass
+// the array's name to a kernel -- on the host that name is only a stand-in -- so the first
+// call on each device looks the device address up with cudaGetSymbolAddress (that device
+// current) and caches it; make that first call before any stream capture. Every call
+// shares the array and it keeps the last call's partials, so calls that overlap on the GPU
+// (two streams, or two host threads) race; serialise them. Requests needing more than
+// kNoAllocScratchFloats partials (filters * ceil(batch*spatial / 32768)) are rejected.
+// --------------------------------------------------------------------------------------
+
+namespace dnb {
+namespace {
+
+constexpr int64_t kNoAllocScratchFloats = 1 << 18;
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
+
+constexpr int kNoAllocMaxDevices = 64;
+float *g_noalloc_ptr[kNoAllocMaxDevices] = {};
+std::once_flag g_noalloc_once[kNoAllocMaxDevices];
+cudaError_t g_noalloc_err[kNoAllocMaxDevices] = {};
+
+// Device address of the scratch array on the current device (looked up once per device).
+dnb_status noalloc_scratch(float **out) {
+    int device = 0;
+    DNB_CUDA(cudaGetDevice(&device));
+    if (device < 0 || device >= kNoAllocMaxDevices)
+        return fail(DNB_ERR_UNSUPPORTED, "mean_noalloc: device %d beyond %d", device, kNoAllocMaxDevices);
+    std::call_once(g_noalloc_once[device], [device] {
+        void *p = nullptr;
+        g_noalloc_err[device] = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (g_noalloc_err[device] == cudaSuccess) g_noalloc_ptr[device] = static_cast<float *>(p);
+    });
+    if (g_noalloc_err[device] != cudaSuccess)
+        return cuda_fail(g_noalloc_err[device], "cudaGetSymbolAddress(g_noalloc_scratch)", __FILE__, __LINE__);
+    *out = g_noalloc_ptr[device];
+    return DNB_OK;
+}
+
+}  // namespace
+}  // namespace dnb
+
+extern "C" dnb_status dnb_mean_noalloc(const float *x, int64_t batch, int64_t filters, int64_t spatial, float *out,
+                                       dnb_stream stream) {
+    using namespace dnb;
+    const char *what = "mean_noalloc";
+    if (batch < 0 || filters < 0 || spatial < 0) return fail(DNB_ERR_INVALID, "%s: negative size", what);
+    if (filters == 0) return DNB_OK;
+    if (!out || (batch * spatial > 0 && !x)) return fail(DNB_ERR_INVALID, "%s: null pointer", what);
+    if (filters > 65535) return fail(DNB_ERR_UNSUPPORTED, "%s: more than 65535 channels", what);
+    // the geometry dnb_mean uses (chan_reduce), so both produce the same partials
+    Geometry g;
+    g.batch = batch;
+    g.filters = filters;
+    g.spatial = spatial;
+    g.per_channel = batch * spatial;
+    g.vec = spatial % 4 == 0 && aligned16(x);
+    g.chunk = kChunkElems;
+    int64_t chunks = (g.per_channel + g.chunk - 1) / g.chunk;
+    if (chunks < 1) chunks = 1;
+    g.chunks = (int)chunks;
+    g.fast = g.per_channel < (1ll << 32);
+    if (spatial > 0) {
+        g.fs = FastDiv((uint32_t)(g.fast ? spatial : 1));
+        g.fs4 = FastDiv((uint32_t)(g.fast && g.vec ? spatial / 4 : 1));
+    }
+    if (filters * chunks > kNoAllocScratchFloats)
+        return fail(DNB_ERR_UNSUPPORTED,
+                    "%s: needs %lld partial sums (filters * ceil(batch*spatial/%lld)); the fixed scratch holds %lld",
+                    what, (long long)(filters * chunks), (long long)kChunkElems, (long long)kNoAllocScratchFloats);
+    float *partial = nullptr;
+    DNB_TRY(noalloc_scratch(&partial));
+    const cudaStream_t s = as_stream(stream);
+    if (g.per_channel > 0) {
+        k_chan_partial<TermSum, false><<<dim3((unsigned)chunks, (unsigned)filters), kThreads, 0, s>>>(g, x, nullptr,
+                                                                                                   nullptr, partial);
+    } else {
+        // the previous call's partials are still there: clear the slots this call reads
+        DNB_CUDA(cudaMemsetAsync(partial, 0, sizeof(float) * (size_t)(filters * chunks), s));
+    }
+    DNB_CUDA(cudaGetLastError());
+    const float scale = 1.0f / (float)(batch * spatial);  // blas.zig:107
+    const unsigned warps_per_block = 8;
+    const unsigned blocks = (unsigned)((filters + warps_per_block - 1) / warps_per_block);
+    k_chan_close<<<blocks, 32 * warps_per_block, 0, s>>>(filters, g.chunks, partial, Close::Mean, scale, nullptr, out);
+    DNB_CUDA(cudaGetLastError());
+    return DNB_OK;
+}

@@ -245,6 +245,17 @@ dnb_status dnb_sgd_momentum(int64_t n, float *weights, float *weight_updates, fl
 dnb_status dnb_softmax_xent(const float *input, const float *truth, int64_t n, int64_t batch, float temp,
                             float *output, float *delta, float *err, float *cost, dnb_stream stream);
 
+/* dnb_mean without any device allocation. No counterpart in the reference: it exists for
+ * callers that may not call cudaMalloc on this path (a pre-budgeted memory pool or arena,
+ * a fixed memory plan between its creation and its replay, a runtime that owns the
+ * allocator). Same result as dnb_mean; its partial sums live in a fixed 1 MiB array inside
+ * the library, held by every GPU that loads it. Limit: filters * ceil(batch*spatial/32768)
+ * <= 262144, else DNB_ERR_UNSUPPORTED. The first call on a device looks up that array's
+ * address; make it before any stream capture. Calls share the array: calls that overlap on
+ * the GPU race, so serialise them. */
+dnb_status dnb_mean_noalloc(const float *x, int64_t batch, int64_t filters, int64_t spatial, float *out,
+                            dnb_stream stream);
+
 /* ------------------------------------------------------------------------------------ */
 /* sync-BN across GPUs (the reference has no multi-GPU support, README.md:313-317).        */
 /* Split form for a caller that owns the collective (e.g. NCCL): each rank computes its    */
