@@ -11,11 +11,19 @@ on NCHW fp32 [128,128,32,32] per GPU (16.8 M elements, 64 MiB per tensor). With 
 every rank holds its own 128-image shard and the per-channel statistics are combined
 across ranks each step (sync-BN, global batch 128*N): weak scaling.
 
-Timing: W untimed steps, then K steps, each kernel preceded by an untimed write of a
-256 MiB buffer (larger than the 126 MB L2) so every timed kernel starts cold; CUDA events
-on the launching stream bracket each kernel; a barrier and a synchronize bracket the K
-steps; the reported time is the maximum over ranks. `value` is the algorithmic bytes of
-all ranks (20 B per element per step) divided by that time.
+Timing: W untimed steps, then three timed regions of K launches each: K whole steps
+(forward on set k, backward on set k+1), K forwards, K backwards. Every kernel starts with
+a cold L2: by default the launches rotate through 3 sets of (x, delta, y, dx) (768 MiB at
+the default shape, more than twice the 126 MB L2), so a launch's tensors were last touched
+hundreds of MB of traffic earlier and each kernel also writes back its predecessor's dirty
+outputs, as in a training step; the launches of a region run back to back between one
+pair of CUDA events on the launching stream (a GPU-side spin before the region lets the
+host queue them all first). `--flush read|write` instead runs an untimed read (or write)
+of a 256 MiB buffer before each launch and brackets every launch with its own events.
+`ms_per_step` is the step region's time per step, the kernel figures come from the other
+two; a barrier and a synchronize bracket each region and the times are the maximum over
+ranks. `value` is the algorithmic bytes of all ranks (20 B per element per step) divided
+by the step time.
 
 `e2e` repeats the step through the C ABI with HOST buffers: x and delta are copied in
 from pinned memory and y and dx copied out every step, inside the timed region.
@@ -53,6 +61,11 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--shape", default="128,128,32,32", help="per-GPU batch,channels,height,width")
+    ap.add_argument("--flush", choices=["rotate", "read", "write"], default="rotate",
+                    help="cold L2 for every timed kernel: rotate through sets of tensors larger than L2 "
+                         "together, with no flush kernel (each kernel also writes back the previous "
+                         "one's dirty outputs, as in a training step); or read a 256 MiB buffer before "
+                         "each kernel (L2 left clean); or write one (L2 left full of dirty lines)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     a = ap.parse_args()
@@ -196,56 +209,89 @@ def run_ours(a):
     dev = torch.device("cuda", local)
     g = torch.Generator(device=dev)
     g.manual_seed(1234 + rank)
-    x = torch.randn(E, generator=g, device=dev)
-    delta = torch.randn(E, generator=g, device=dev)
+    # rotate: enough sets of (x, delta, y, dx) that a step's tensors were last touched more
+    # than two L2 capacities (2 x 126 MB) of traffic earlier
+    n_sets = 1 if a.flush != "rotate" else max(2, -(-(3 * 126 * 2**20) // (4 * E * 4)) + 1)
+    sets = []
+    for _ in range(n_sets):
+        sx = torch.randn(E, generator=g, device=dev)
+        sd = torch.randn(E, generator=g, device=dev)
+        sets.append((sx, sd, torch.empty_like(sx), torch.empty_like(sx)))
+    x, delta, y, dx = sets[0]
     gamma = torch.rand(C, generator=g, device=dev) + 0.5
     beta = torch.randn(C, generator=g, device=dev) * 0.1
-    y = torch.empty_like(x)
-    dx = torch.empty_like(x)
     mean, var, rm, rv, bu, su, md, vd = (torch.zeros(C, device=dev) for _ in range(8))
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    flush_buf = torch.ones(64 << 20, dtype=torch.float32, device=dev) if a.flush != "rotate" else None
+
+    def flush():
+        if a.flush == "read":
+            flush_buf.sum()
+        elif a.flush == "write":
+            flush_buf.fill_(1.0)
+
     layer = syncbn.SyncBN(B, C, S, world=world, dist=dist)
 
-    def fwd():
-        layer.forward(x, y, gamma, beta, mean, var, rm, rv, LEAKY)
+    def fwd(k):
+        sx, sd, sy, sdx = sets[k % n_sets]
+        layer.forward(sx, sy, gamma, beta, mean, var, rm, rv, LEAKY)
 
-    def bwd():
-        layer.backward(x, delta, dx, gamma, beta, mean, var, bu, su, md, vd, LEAKY)
+    def bwd(k):
+        # the backward of a step works on the next set: its x was last touched a whole
+        # rotation earlier, as a layer's backward comes long after its forward
+        sx, sd, sy, sdx = sets[(k + 1) % n_sets]
+        layer.backward(sx, sd, sdx, gamma, beta, mean, var, bu, su, md, vd, LEAKY)
 
     stream = torch.cuda.current_stream()
-    for _ in range(a.warmup):
-        flush.zero_()
-        fwd()
-        flush.zero_()
-        bwd()
+    for k in range(a.warmup):
+        flush()
+        fwd(k)
+        flush()
+        bwd(k)
     torch.cuda.synchronize()
     gpu.check_device_error()
 
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(a.steps)]
+    def timed(body):
+        """Device time of body(k) for k < steps, in ms per k (max over ranks by the caller).
+        A GPU-side spin first lets the host queue every launch before the GPU reaches them,
+        so no interval contains time the GPU waited for the host."""
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+        torch.cuda._sleep(int(0.25e-3 * 2e9) * a.steps)
+        if a.flush == "rotate":
+            # back-to-back launches between one pair of events
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for k in range(a.steps):
+                body(k)
+            e1.record(stream)
+            torch.cuda.synchronize()
+            return e0.elapsed_time(e1) / a.steps
+        # a flush kernel before every launch: one pair of events per launch
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(a.steps)]
+        for k in range(a.steps):
+            flush()
+            ev[k][0].record(stream)
+            body(k)
+            ev[k][1].record(stream)
+        torch.cuda.synchronize()
+        return sum(e0.elapsed_time(e1) for e0, e1 in ev) / a.steps
+
     clocks = ClockSampler(local)
     clocks.start()
-    if dist:
-        dist.barrier()
-    torch.cuda.synchronize()
-    for k in range(a.steps):
-        flush.zero_()
-        ev[k][0].record(stream)
-        fwd()
-        ev[k][1].record(stream)
-        flush.zero_()
-        ev[k][2].record(stream)
-        bwd()
-        ev[k][3].record(stream)
-    torch.cuda.synchronize()
+    launches0 = gpu.launch_count()
+    if a.flush == "rotate":
+        ms_step = timed(lambda k: (fwd(k), bwd(k)))
+    launches = gpu.launch_count() - launches0
+    ms_fwd = timed(fwd)
+    ms_bwd = timed(bwd)
+    if a.flush != "rotate":
+        ms_step = ms_fwd + ms_bwd
+        launches = gpu.launch_count() - launches0  # K forward + K backward launches
     if dist:
         dist.barrier()
     clk = clocks.stop()
     gpu.check_device_error()
-    t_fwd = [e[0].elapsed_time(e[1]) for e in ev]
-    t_bwd = [e[2].elapsed_time(e[3]) for e in ev]
-    ms_fwd = sum(t_fwd) / a.steps
-    ms_bwd = sum(t_bwd) / a.steps
-    ms_step = ms_fwd + ms_bwd
     if dist:
         t = torch.tensor([ms_step, ms_fwd, ms_bwd], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -255,7 +301,6 @@ def run_ours(a):
     if not a.no_e2e:
         e2e = run_e2e(a, layer, x, y, delta, dx, gamma, beta, mean, var, rm, rv, bu, su, md, vd, dev, dist, world)
 
-    launches_per_step = layer.launches_per_step()
     if dist:
         # release NCCL state before the process group goes away
         dist.barrier()
@@ -283,7 +328,12 @@ def run_ours(a):
         "data": "synthetic (torch.randn / rand, seeded per rank)",
         "config": {"workload": workload_desc(a.shape, world), "batch_per_gpu": B, "channels": C, "hw": [H, W],
                    "global_batch": B * world, "activation": "leaky 0.1",
-                   "l2": "256 MiB buffer written before every timed kernel (cold L2); 64 MiB tensors",
+                   "l2": (f"rotating {n_sets} sets of (x, delta, y, dx), {n_sets * 4 * E * 4 / 2**20:.0f} MiB "
+                          f"> 2 x 126 MB L2: every kernel starts cold and writes back its predecessor's "
+                          f"outputs" if a.flush == "rotate" else
+                          f"256 MiB buffer {'read' if a.flush == 'read' else 'written'} before every timed "
+                          f"kernel (cold L2{'' if a.flush == 'read' else ', full of dirty lines'})")
+                         + f"; {E * 4 / 2**20:.0f} MiB tensors",
                    "parallelism": f"dp{world}" + (" + sync-BN" if world > 1 else "")},
         "elems_per_s": round(E * world / (ms_step * 1e-3), 1),
         "pct_of_8TBs": round(100.0 * value / world / HBM_NOMINAL_GBS, 2),
@@ -298,7 +348,7 @@ def run_ours(a):
                      else "fallback 6.65 TB/s", "unit": "GB/s", "frac": round(bwd_gbs / peak, 4),
                      "traffic": (traffic or {}).get("bwd_dram_bytes_per_launch"),
                      "algorithmic_bytes": BYTES_BWD * E},
-        "gpu_launches": launches_per_step * a.steps,
+        "gpu_launches": launches,
         "clocks": clk,
     }
     if e2e:

@@ -469,6 +469,8 @@ struct PArgs {
     int act;
     float4 *rec;              // [G][Ps][2 segments]
     uint32_t step_q, step_r;  // kLThreads float4s = step_q units + step_r float4s
+    int cpu;                  // sweep: chunks per unit
+    FastDiv f_cpu;
     unsigned *sync;           // [0] epoch, then 2 banks of {stats_done[kMaxGroups], apply_done[kMaxGroups]}
     unsigned *err, *abort_flag;
     unsigned long long wait_ns;
@@ -1233,6 +1235,635 @@ dnb_status run_persistent(int64_t batch, int64_t filters, int64_t spatial, int a
     });
 }
 
+// ======================================================================================
+// persistent fused kernel, single role: the sweep
+// ======================================================================================
+//
+// Every CTA owns the same balanced share of each channel group in both passes, and its
+// warps are split in two. The 15 streaming warps reduce group g+1 (HBM reads) and then
+// write group g's outputs (its share re-read from L2); they never touch global
+// synchronisation. The control warp takes group g's per-warp partials from shared memory,
+// publishes the CTA's records, counts the CTA in stats_done[g], waits until every CTA has
+// done so, merges the records of the share's channels and hands the apply parameters back
+// through shared memory -- all while the streaming warps reduce group g+1, so the latency
+// of the grid-wide exchange (several L2 round trips behind saturated memory pipes) stays
+// off the streaming path. Statistics loads carry an L2 evict_last policy, output-pass loads
+// and stores evict_first, so a group stays in L2 between its two passes; groups are sized
+// so that two fit in L2. Every global wait is bounded; on timeout the control warp sets
+// the device error word and tells the streaming warps to stop.
+
+constexpr int kSThreads = 512;              // threads of a sweep CTA
+constexpr int kSMinBlocks = 2;              // CTAs per SM the register budget is set for
+constexpr int kSWarps = kSThreads / 32 - 1;  // streaming warps; the last warp is the control warp
+
+__device__ __forceinline__ uint64_t l2_evict_last() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, %1;" : "=l"(p) : "f"(1.0f));
+    return p;
+}
+__device__ __forceinline__ uint64_t l2_evict_first() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, %1;" : "=l"(p) : "f"(1.0f));
+    return p;
+}
+__device__ __forceinline__ float4 ld4_hint(const float *p, uint64_t pol) {
+    float4 v;
+    asm volatile("ld.global.L1::no_allocate.L2::cache_hint.v4.f32 {%0, %1, %2, %3}, [%4], %5;"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "l"(p), "l"(pol));
+    return v;
+}
+__device__ __forceinline__ void st4_hint(float *p, float4 v, uint64_t pol) {
+    asm volatile("st.global.L1::no_allocate.L2::cache_hint.v4.f32 [%0], {%1, %2, %3, %4}, %5;" ::"l"(p), "f"(v.x),
+                 "f"(v.y), "f"(v.z), "f"(v.w), "l"(pol)
+                 : "memory");
+}
+// Named CTA barriers: bar_sync waits for `count` threads, bar_arrive counts without waiting.
+// The non-aligned forms count threads one by one, so a warp whose lanes reach the barrier
+// apart (after lane-dependent code) is still counted once per thread; the __syncwarp
+// brings the lanes together first anyway.
+__device__ __forceinline__ void bar_sync(int id, int count) {
+    __syncwarp();
+    asm volatile("barrier.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+__device__ __forceinline__ void bar_arrive(int id, int count) {
+    __syncwarp();
+    asm volatile("barrier.arrive %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+// barrier ids: 1,2 = stats of group g done (g & 1); 3,4 = parameters of group g ready;
+// 5 = the streaming warps among themselves
+constexpr int kBarStats = 1, kBarParams = 3, kBarStream = 5;
+constexpr int kStreamThreads = kSWarps * 32;
+
+template <bool BWD, int A, bool HASY>
+struct SweepKernel {
+    using PK = PipeKernel<BWD, A, HASY>;
+    static constexpr int UNROLL = BWD ? 2 : 4;  // float4s per tensor in flight per thread
+    static constexpr int CHUNK = 32 * UNROLL;   // float4s of one unit a warp takes at a time
+
+    struct Smem {
+        uint32_t *utab;  // [2][cap_units] element offset of each unit of the share (< 2^32)
+        float4 *wrec;    // [2 buffers][2 segments][kSWarps] per-warp partials
+        float *ptab;     // [2 buffers][2 segments][8] apply parameters
+        float4 *stab;    // [2 buffers][2 segments] forward parameters for the backward's stats
+        int *stop;       // set by the control warp when a wait gave up
+    };
+    __host__ __device__ static size_t smem_bytes(int cap_units) {
+        return (((size_t)2 * cap_units * sizeof(uint32_t) + 15) & ~(size_t)15) + 4 * kSWarps * sizeof(float4) +
+               32 * sizeof(float) + 4 * sizeof(float4) + 16;
+    }
+    __device__ static Smem carve(const PArgs &a, unsigned char *raw) {
+        Smem s;
+        size_t o = 0;
+        s.utab = reinterpret_cast<uint32_t *>(raw);
+        o += ((size_t)2 * a.cap_units * sizeof(uint32_t) + 15) & ~(size_t)15;
+        s.wrec = reinterpret_cast<float4 *>(raw + o);
+        o += 4 * kSWarps * sizeof(float4);
+        s.ptab = reinterpret_cast<float *>(raw + o);
+        o += 32 * sizeof(float);
+        s.stab = reinterpret_cast<float4 *>(raw + o);
+        o += 4 * sizeof(float4);
+        s.stop = reinterpret_cast<int *>(raw + o);
+        return s;
+    }
+
+    // streaming warps: element offsets of the units of CTA rid's share of group g into
+    // table b (and, for the backward, the forward parameters of its segments)
+    __device__ static void tabulate(const PArgs &a, const Smem &s, int g, int rid, int b) {
+        const Share sh = share_of(a, g, rid, a.f_ps);
+        const int n_units = (int)(sh.t1 - sh.t0);
+        for (int u = threadIdx.x; u < n_units; u += kStreamThreads) {
+            uint32_t cl, rem, n, k;
+            a.f_nk.divmod(sh.t0 + u, cl, rem);
+            a.f_k.divmod(rem, n, k);
+            s.utab[b * a.cap_units + u] = (uint32_t)(((int64_t)n * a.C + sh.c0 + cl) * a.S + (int64_t)k * a.U);
+        }
+        if (BWD && threadIdx.x < sh.nseg) {
+            const BwdParam p = PK::fwd_params_of(a, (int64_t)sh.c0 + sh.cfirst + threadIdx.x);
+            s.stab[2 * b + threadIdx.x] = make_float4(p.m, p.inv, p.g, p.b);
+        }
+    }
+
+    // The share is cut into chunks of CHUNK float4s of one unit (a unit is a.cpu chunks, the
+    // last one possibly partial); streaming warp w takes chunks w, w + kSWarps, ... Lane l
+    // of a chunk starting at float4 k0 of its unit holds float4s k0 + l + 32 j, j < UNROLL.
+    // A warp's chunks run through the share in order, so its segment changes at most once.
+    struct Chunk {
+        uint32_t off;  // element offset of the lane's first float4
+        uint32_t k;    // index of that float4 within the unit
+        int seg;
+    };
+    __device__ static Chunk chunk_at(const PArgs &a, const Share &sh, const uint32_t *ut, uint32_t c, int lane) {
+        uint32_t uo, part;
+        a.f_cpu.divmod(c, uo, part);
+        Chunk ch;
+        ch.k = part * CHUNK + lane;
+        ch.off = ut[uo] + 4 * ch.k;
+        ch.seg = sh.t0 + uo >= sh.bnd ? 1 : 0;
+        return ch;
+    }
+
+    // streaming warps: statistics of CTA rid's share of group g (table b); each warp leaves
+    // one partial per segment in s.wrec[b]
+    __device__ static void stats(const PArgs &a, const Smem &s, int g, int rid, int b) {
+        const Share sh = share_of(a, g, rid, a.f_ps);
+        const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+        const uint32_t u4 = (uint32_t)a.U >> 2;
+        const uint32_t n_chunks = sh.nseg ? (sh.t1 - sh.t0) * (uint32_t)a.cpu : 0;
+        const uint32_t *ut = s.utab + b * a.cap_units;
+        const uint64_t pol = l2_evict_last();
+        float4 rec[2];
+        int seg = 0;
+        if constexpr (!BWD) {
+            Moments mo;
+            float4 first = make_float4(0.0f, 0.0f, 0.0f, 0.0f);  // segment 0 once the warp moved on
+            for (uint32_t c = warp; c < n_chunks; c += kSWarps) {
+                const Chunk ch = chunk_at(a, sh, ut, c, lane);
+                if (ch.seg != seg) {  // warp-uniform
+                    first = mo.warp_summary();
+                    mo = Moments();
+                    seg = ch.seg;
+                }
+                const float *p = a.t0 + ch.off;
+                float4 v[UNROLL];
+#pragma unroll
+                for (int j = 0; j < UNROLL; ++j)
+                    if (ch.k + 32 * j < u4) v[j] = ld4_hint(p + 128 * j, pol);
+#pragma unroll
+                for (int j = 0; j < UNROLL; ++j)
+                    if (ch.k + 32 * j < u4) mo.add4(v[j]);
+            }
+            const float4 last = mo.warp_summary();
+            rec[0] = seg ? first : last;
+            rec[1] = seg ? last : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        } else {
+            float s1 = 0.0f, s2 = 0.0f, f1 = 0.0f, f2 = 0.0f;  // f: segment 0 once the warp moved on
+            for (uint32_t c = warp; c < n_chunks; c += kSWarps) {
+                const Chunk ch = chunk_at(a, sh, ut, c, lane);
+                if (ch.seg != seg) {
+                    f1 = s1;
+                    f2 = s2;
+                    s1 = s2 = 0.0f;
+                    seg = ch.seg;
+                }
+                const float4 fp = s.stab[2 * b + seg];  // warp-uniform broadcast
+                BwdParam p;
+                p.m = fp.x;
+                p.inv = fp.y;
+                p.g = fp.z;
+                p.b = fp.w;
+                float4 d[UNROLL], xv[UNROLL], yv[UNROLL];
+#pragma unroll
+                for (int j = 0; j < UNROLL; ++j)
+                    if (ch.k + 32 * j < u4) {
+                        d[j] = ld4_hint(a.t0 + ch.off + 128 * j, pol);
+                        xv[j] = ld4_hint(a.t1 + ch.off + 128 * j, pol);
+                        if (HASY) yv[j] = ld4_hint(a.t2 + ch.off + 128 * j, pol);
+                    }
+#pragma unroll
+                for (int j = 0; j < UNROLL; ++j)
+                    if (ch.k + 32 * j < u4) {
+                        const float4 yy = HASY ? yv[j] : xv[j];
+                        const float g0 = bn_grad1<A, HASY>(d[j].x, xv[j].x, yy.x, p, a.act);
+                        const float g1 = bn_grad1<A, HASY>(d[j].y, xv[j].y, yy.y, p, a.act);
+                        const float g2 = bn_grad1<A, HASY>(d[j].z, xv[j].z, yy.z, p, a.act);
+                        const float g3 = bn_grad1<A, HASY>(d[j].w, xv[j].w, yy.w, p, a.act);
+                        s1 += (g0 + g1) + (g2 + g3);
+                        s2 += (g0 * (xv[j].x - p.m) + g1 * (xv[j].y - p.m)) +
+                              (g2 * (xv[j].z - p.m) + g3 * (xv[j].w - p.m));
+                    }
+            }
+            const float t1 = warp_sum(s1), t2 = warp_sum(s2);
+            const float u1 = warp_sum(f1), u2 = warp_sum(f2);
+            rec[0] = seg ? make_float4(u1, u2, 0.0f, 0.0f) : make_float4(t1, t2, 0.0f, 0.0f);
+            rec[1] = seg ? make_float4(t1, t2, 0.0f, 0.0f) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        }
+        if (lane == 0) {
+            s.wrec[(2 * b + 0) * kSWarps + warp] = rec[0];
+            s.wrec[(2 * b + 1) * kSWarps + warp] = rec[1];
+        }
+    }
+
+    // control warp: one record per segment from the streaming warps' partials of group g
+    // (buffer b), written to a.rec; lane 0 then publishes them and counts the CTA
+    __device__ static void publish(const PArgs &a, const Smem &s, int g, int rid, int b, unsigned *stats_done) {
+        const Share sh = share_of(a, g, rid, a.f_ps);
+        const int lane = threadIdx.x & 31;
+        for (int j = 0; j < sh.nseg; ++j) {
+            float4 q = lane < kSWarps ? s.wrec[(2 * b + j) * kSWarps + lane] : make_float4(0, 0, 0, 0);
+            if constexpr (!BWD) {
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    const float cb = __shfl_xor_sync(0xffffffffu, q.x, o);
+                    const float mb = __shfl_xor_sync(0xffffffffu, q.y, o);
+                    const float qb = __shfl_xor_sync(0xffffffffu, q.z, o);
+                    chan_merge(q.x, q.y, q.z, cb, mb, qb);
+                }
+            } else {
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    q.x += __shfl_xor_sync(0xffffffffu, q.x, o);
+                    q.y += __shfl_xor_sync(0xffffffffu, q.y, o);
+                }
+            }
+            if (lane == 0) a.rec[((int64_t)g * a.Ps + rid) * 2 + j] = q;
+        }
+        // lane 0 wrote every record: its release-add publishes them
+        if (lane == 0) asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(stats_done + g) : "memory");
+        __syncwarp();
+    }
+
+    // control warp: bounded wait until every CTA counted itself in stats_done[g]
+    __device__ static bool wait_all(const PArgs &a, const unsigned *stats_done, int g) {
+        int ok = 1;
+        if ((threadIdx.x & 31) == 0) {
+            const unsigned *cnt = stats_done + g;
+            if (ld_acquire_gpu(cnt) < (unsigned)a.Ps) {
+                const unsigned long long deadline = global_ns() + a.wait_ns;
+                while (ld_acquire_gpu(cnt) < (unsigned)a.Ps) {
+                    if (ld_volatile(a.abort_flag)) {
+                        ok = 0;
+                        break;
+                    }
+                    if (global_ns() > deadline) {
+                        atomicOr(a.err, DEVERR_WAIT_BARRIER);
+                        atomicExch(a.abort_flag, 1u);
+                        ok = 0;
+                        break;
+                    }
+                    __nanosleep(64);
+                }
+            }
+        }
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        __syncwarp();  // lane 0's acquire orders the other lanes' record loads too
+        return ok != 0;
+    }
+
+    // control warp: merge the records of the (at most two) channels of CTA rid's share of
+    // group g into the apply parameters s.ptab[b]; the CTA owning a channel's first unit
+    // writes the per-channel outputs. Records of CTAs between the channel's first and last
+    // owner that hold no unit of it (a group with fewer units than CTAs) are skipped.
+    __device__ static void merge(const PArgs &a, const Smem &s, int g, int rid, int b) {
+        const Share sh = share_of(a, g, rid, a.f_ps);
+        const int lane = threadIdx.x & 31;
+        for (int j = 0; j < sh.nseg; ++j) {
+            const int cl = sh.cfirst + j;
+            const int64_t c = (int64_t)sh.c0 + cl;
+            float gamma = 0.0f, beta = 0.0f, m_in = 0.0f, v_in = 0.0f, rm = 0.0f, rv = 0.0f;
+            const uint32_t ua = (uint32_t)cl * a.NK, ub = ua + a.NK;
+            const bool write = owner_of(a, g, ua, a.Ps) == rid;
+            if (lane == 0) {
+                gamma = a.scales[c];
+                beta = a.biases[c];
+                if constexpr (BWD) {
+                    m_in = a.mean_in[c];
+                    v_in = a.var_in[c];
+                } else if (write) {
+                    rm = a.rmean[c];
+                    rv = a.rvar[c];
+                }
+            }
+            const int plo = owner_of(a, g, ua, a.Ps), phi = owner_of(a, g, ub - 1, a.Ps);
+            const int nrec = phi - plo + 1;
+            auto load = [&](int idx, float4 &dst) -> bool {
+                const int p = plo + idx;
+                const Share o = share_of(a, g, p, a.f_ps);
+                const uint32_t lo = ua > o.t0 ? ua : o.t0, hi = ub < o.t1 ? ub : o.t1;
+                if (hi <= lo) return false;
+                dst = __ldcg(&a.rec[((int64_t)g * a.Ps + p) * 2 + (cl - o.cfirst)]);
+                return true;
+            };
+            constexpr int R = 2;  // records held per lane: one L2 round trip up to 64 records
+            float4 r[R];
+            bool have[R];
+#pragma unroll
+            for (int k = 0; k < R; ++k) {
+                const int idx = lane + 32 * k;
+                have[k] = idx < nrec && load(idx, r[k]);
+            }
+            float *out = s.ptab + (2 * b + j) * 8;
+            if constexpr (!BWD) {
+                double sn = 0.0, smn = 0.0;
+#pragma unroll
+                for (int k = 0; k < R; ++k)
+                    if (have[k]) {
+                        sn += (double)r[k].x;
+                        smn += (double)r[k].x * (double)r[k].y;
+                    }
+                for (int idx = lane + 32 * R; idx < nrec; idx += 32) {
+                    float4 t;
+                    if (!load(idx, t)) continue;
+                    sn += (double)t.x;
+                    smn += (double)t.x * (double)t.y;
+                }
+                sn = warp_sum(sn);
+                const double mu = warp_sum(smn) / sn;
+                double m2 = 0.0;
+#pragma unroll
+                for (int k = 0; k < R; ++k)
+                    if (have[k]) {
+                        const double d = (double)r[k].y - mu;
+                        m2 += (double)r[k].z + (double)r[k].x * d * d;
+                    }
+                for (int idx = lane + 32 * R; idx < nrec; idx += 32) {
+                    float4 t;
+                    if (!load(idx, t)) continue;
+                    const double d = (double)t.y - mu;
+                    m2 += (double)t.z + (double)t.x * d * d;
+                }
+                m2 = warp_sum(m2);
+                if (lane == 0) {
+                    const FwdClose f = fwd_close(mu, m2, sn);
+                    if (write) {
+                        a.mean[c] = f.m;
+                        a.var[c] = f.var;
+                        a.rmean[c] = rolling(rm, f.m);
+                        a.rvar[c] = rolling(rv, f.var);
+                    }
+                    *reinterpret_cast<float4 *>(out) = make_float4(f.m, f.inv, gamma, beta);
+                }
+            } else {
+                double s1 = 0.0, s2 = 0.0;
+#pragma unroll
+                for (int k = 0; k < R; ++k)
+                    if (have[k]) {
+                        s1 += (double)r[k].x;
+                        s2 += (double)r[k].y;
+                    }
+                for (int idx = lane + 32 * R; idx < nrec; idx += 32) {
+                    float4 t;
+                    if (!load(idx, t)) continue;
+                    s1 += (double)t.x;
+                    s2 += (double)t.y;
+                }
+                s1 = warp_sum(s1);
+                s2 = warp_sum(s2);
+                if (lane == 0) {
+                    const BwdParam bp = bwd_close(s1, s2, m_in, v_in, gamma, beta, a.denom, a.bias_upd, a.scale_upd,
+                                                  a.mean_delta, a.var_delta, c, write);
+                    *reinterpret_cast<BwdParam *>(out) = bp;
+                }
+            }
+        }
+        __syncwarp();
+    }
+
+    // streaming warps: outputs of CTA rid's share of group g (table b, parameters s.ptab[b])
+    __device__ static void apply(const PArgs &a, const Smem &s, int g, int rid, int b) {
+        const Share sh = share_of(a, g, rid, a.f_ps);
+        if (sh.nseg == 0) return;
+        const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+        const uint32_t u4 = (uint32_t)a.U >> 2;
+        const uint32_t n_chunks = (sh.t1 - sh.t0) * (uint32_t)a.cpu;
+        const uint32_t *ut = s.utab + b * a.cap_units;
+        const float *ptab = s.ptab + 16 * b;
+        const uint64_t pol = l2_evict_first();
+        if constexpr (!BWD) {
+            for (uint32_t c = warp; c < n_chunks; c += kSWarps) {
+                const Chunk ch = chunk_at(a, sh, ut, c, lane);
+                const float4 p = *reinterpret_cast<const float4 *>(ptab + 8 * ch.seg);
+                float4 v[UNROLL];
+#pragma unroll
+                for (int j = 0; j < UNROLL; ++j)
+                    if (ch.k + 32 * j < u4) v[j] = ld4_hint(a.t0 + ch.off + 128 * j, pol);
+#pragma unroll
+                for (int j = 0; j < UNROLL; ++j)
+                    if (ch.k + 32 * j < u4) {
+                        const uint32_t off = ch.off + 128 * j;
+                        if (a.xnorm)
+                            st4_hint(a.xnorm + off,
+                                     make_float4((v[j].x - p.x) * p.y, (v[j].y - p.x) * p.y, (v[j].z - p.x) * p.y,
+                                                 (v[j].w - p.x) * p.y),
+                                     pol);
+                        st4_hint(a.out + off,
+                                 make_float4(bn_fwd1<A>(v[j].x, p.x, p.y, p.z, p.w, a.act),
+                                             bn_fwd1<A>(v[j].y, p.x, p.y, p.z, p.w, a.act),
+                                             bn_fwd1<A>(v[j].z, p.x, p.y, p.z, p.w, a.act),
+                                             bn_fwd1<A>(v[j].w, p.x, p.y, p.z, p.w, a.act)),
+                                 pol);
+                    }
+            }
+        } else {
+            for (uint32_t c = warp; c < n_chunks; c += kSWarps) {
+                const Chunk ch = chunk_at(a, sh, ut, c, lane);
+                const BwdParam p = *reinterpret_cast<const BwdParam *>(ptab + 8 * ch.seg);
+                float4 d[UNROLL], xv[UNROLL], yv[UNROLL];
+#pragma unroll
+                for (int j = 0; j < UNROLL; ++j)
+                    if (ch.k + 32 * j < u4) {
+                        d[j] = ld4_hint(a.t0 + ch.off + 128 * j, pol);
+                        xv[j] = ld4_hint(a.t1 + ch.off + 128 * j, pol);
+                        if (HASY) yv[j] = ld4_hint(a.t2 + ch.off + 128 * j, pol);
+                    }
+#pragma unroll
+                for (int j = 0; j < UNROLL; ++j)
+                    if (ch.k + 32 * j < u4) {
+                        const float4 yy = HASY ? yv[j] : xv[j];
+                        st4_hint(a.out + ch.off + 128 * j,
+                                 make_float4(bn_dx_p(bn_grad1<A, HASY>(d[j].x, xv[j].x, yy.x, p, a.act), xv[j].x, p, a),
+                                             bn_dx_p(bn_grad1<A, HASY>(d[j].y, xv[j].y, yy.y, p, a.act), xv[j].y, p, a),
+                                             bn_dx_p(bn_grad1<A, HASY>(d[j].z, xv[j].z, yy.z, p, a.act), xv[j].z, p, a),
+                                             bn_dx_p(bn_grad1<A, HASY>(d[j].w, xv[j].w, yy.w, p, a.act), xv[j].w, p, a)),
+                                 pol);
+                    }
+            }
+        }
+    }
+};
+
+template <bool BWD, int A, bool HASY>
+__global__ void __launch_bounds__(kSThreads, kSMinBlocks) k_bn_sweep(PArgs a) {
+    using K = SweepKernel<BWD, A, HASY>;
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    const typename K::Smem s = K::carve(a, smem_raw);
+    __shared__ unsigned s_epoch;
+    if (threadIdx.x == 0) {
+        s_epoch = ld_volatile(&a.sync[0]);
+        *s.stop = 0;
+    }
+    __syncthreads();
+    const unsigned epoch = s_epoch;
+    unsigned *stats_done = a.sync + 1 + (size_t)(epoch & 1u) * 2 * kMaxGroups;
+    const int rid = (int)blockIdx.x;
+    const int warp = threadIdx.x >> 5;
+    if (warp == kSWarps) {
+        // control warp
+        if (rid == 0) {  // the next launch's bank
+            unsigned *other = a.sync + 1 + (size_t)((epoch & 1u) ^ 1u) * 2 * kMaxGroups;
+            for (int i = threadIdx.x & 31; i < 2 * kMaxGroups; i += 32) other[i] = 0u;
+        }
+        for (int g = 0; g < a.G; ++g) {
+            const int b = g & 1;
+            bar_sync(kBarStats + b, kSThreads);  // the streaming warps' partials of group g
+            K::publish(a, s, g, rid, b, stats_done);
+            const bool ok = K::wait_all(a, stats_done, g);
+            // every CTA has read the epoch once all have counted themselves in group 0
+            if (ok && g == 0 && rid == 0 && (threadIdx.x & 31) == 0) atomicExch(&a.sync[0], epoch + 1);
+            if (ok) K::merge(a, s, g, rid, b);
+            else if ((threadIdx.x & 31) == 0) *s.stop = 1;
+            bar_arrive(kBarParams + b, kSThreads);
+            if (!ok) return;
+        }
+        return;
+    }
+    // streaming warps
+    K::tabulate(a, s, 0, rid, 0);
+    bar_sync(kBarStream, kStreamThreads);
+    K::stats(a, s, 0, rid, 0);
+    bar_arrive(kBarStats + 0, kSThreads);
+    for (int g = 0; g < a.G; ++g) {
+        const int b = g & 1;
+        if (g + 1 < a.G) {
+            K::tabulate(a, s, g + 1, rid, b ^ 1);
+            bar_sync(kBarStream, kStreamThreads);
+            K::stats(a, s, g + 1, rid, b ^ 1);
+            bar_arrive(kBarStats + (b ^ 1), kSThreads);
+        }
+        bar_sync(kBarParams + b, kSThreads);  // group g's parameters are in s.ptab[b]
+        if (*s.stop) return;
+        K::apply(a, s, g, rid, b);
+        bar_sync(kBarStream, kStreamThreads);  // table b and s.ptab[b] are rewritten for group g+2
+    }
+}
+
+// Sweep plan: P = 2 CTAs per SM; units of U = spatial/K floats with K the smallest divisor
+// giving >= 8 units per CTA in a group (U >= 256 floats); groups of cg channels whose
+// inputs fill about DNB_BN_GROUP_MB (default 32 MiB) so that the group being written and
+// the group being reduced both stay in L2; cg <= P keeps a share within two channels.
+template <bool BWD, bool HASY>
+PPlan plan_sweep(int64_t batch, int64_t filters, int64_t spatial, const DeviceState *ds, int occupancy) {
+    using K = SweepKernel<BWD, DNB_ACT_LEAKY, HASY>;
+    constexpr int nt = BWD ? (HASY ? 3 : 2) : 1;
+    PPlan pl;
+    if (spatial % 4 != 0 || batch <= 0 || filters <= 0) return pl;
+    int ctas = occupancy < 1 ? 1 : occupancy;
+    if (ctas > 2048 / kSThreads) ctas = 2048 / kSThreads;
+    const int64_t P = (int64_t)ds->sm_count * ctas;
+    const int64_t bytes_per_channel = batch * spatial * 4 * nt;
+    const int64_t budget = (int64_t)env_int("DNB_BN_GROUP_MB", 32, 1, 4096) << 20;
+    int64_t cg = budget / bytes_per_channel;
+    if (cg < 1) cg = 1;
+    if (cg > P) cg = P;
+    if (cg > filters) cg = filters;
+    int64_t G = (filters + cg - 1) / cg;
+    cg = (filters + G - 1) / G;
+    G = (filters + cg - 1) / cg;
+    if (G > kMaxGroups) return pl;
+    int64_t k = 0;
+    for (int64_t kk = 1; kk <= spatial; ++kk) {
+        if (spatial % kk || (spatial / kk) % 4) continue;
+        if (k == 0) k = kk;
+        if (spatial / kk < 256) break;
+        k = kk;
+        if (cg * batch * kk >= 8 * P) break;
+    }
+    if (k == 0) return pl;
+    const int64_t U = spatial / k, NK = batch * k, T = cg * NK;
+    if ((uint64_t)T * (uint64_t)P >= (1ull << 32) - (uint64_t)P) return pl;
+    if ((uint64_t)batch * (uint64_t)filters * (uint64_t)spatial >= (1ull << 32)) return pl;  // 32-bit offsets
+    const int64_t share = (T + P - 1) / P;
+    pl.K = (int)k;
+    pl.U = (int)U;
+    pl.cg = (int)cg;
+    pl.G = (int)G;
+    pl.P = (int)P;
+    pl.depth = 2;
+    pl.cap_units = (int)share;
+    pl.ctas_per_sm = ctas;
+    pl.smem = K::smem_bytes(pl.cap_units);
+    size_t per_cta = (size_t)ds->smem_per_sm / ctas - (size_t)ds->smem_reserved - 256;
+    if (per_cta > (size_t)ds->max_smem_optin) per_cta = (size_t)ds->max_smem_optin;
+    pl.ok = pl.smem <= per_cta;
+    return pl;
+}
+
+// Fills the partition fields of `a` from a plan whose two roles have ps and pa CTAs.
+void fill_partition(PArgs &a, const PPlan &pl, int64_t batch, int64_t filters, int64_t spatial, int ps, int pa,
+                    int threads) {
+    a.C = filters;
+    a.S = spatial;
+    a.N = (int)batch;
+    a.K = pl.K;
+    a.U = pl.U;
+    a.NK = (int)(batch * pl.K);
+    a.cg = pl.cg;
+    a.G = pl.G;
+    a.Ps = ps;
+    a.Pa = pa;
+    a.depth = pl.depth;
+    a.cap_units = pl.cap_units;
+    a.T_full = (uint32_t)pl.cg * (uint32_t)a.NK;
+    a.T_last = (uint32_t)(filters - (int64_t)(pl.G - 1) * pl.cg) * (uint32_t)a.NK;
+    a.f_u4 = FastDiv((uint32_t)(pl.U / 4));
+    a.step_q = (uint32_t)(threads / (pl.U / 4));
+    a.step_r = (uint32_t)(threads % (pl.U / 4));
+    a.f_nk = FastDiv((uint32_t)a.NK);
+    a.f_k = FastDiv((uint32_t)pl.K);
+    a.f_ps = FastDiv((uint32_t)ps);
+    a.f_pa = FastDiv((uint32_t)pa);
+    a.f_tfull = FastDiv(a.T_full);
+    a.f_tlast = FastDiv(a.T_last);
+    a.denom = (float)(spatial * batch);
+    // dividing by a power of two equals multiplying by its exact reciprocal
+    int e2 = 0;
+    a.denom_pow2 = frexpf(a.denom, &e2) == 0.5f;
+    a.inv_denom = 1.0f / a.denom;
+}
+
+template <bool BWD, bool HASY>
+dnb_status run_sweep(int64_t batch, int64_t filters, int64_t spatial, int act, PArgs a, cudaStream_t stream,
+                     bool *launched, const char *what) {
+    *launched = false;
+    DeviceState *ds = nullptr;
+    DNB_TRY(current_device(&ds));
+    return dispatch_act(act, [&]<int A>() -> dnb_status {
+        auto kern = k_bn_sweep<BWD, A, HASY>;
+        // CTAs one SM holds with up to 16 KB of dynamic shared memory (a plan needs less
+        // unless its shares are thousands of units long; checked again below)
+        static int occupancy = -1;
+        if (occupancy < 0) DNB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occupancy, kern, kSThreads, 16384));
+        if (occupancy < 1) return DNB_OK;
+        const PPlan pl = plan_sweep<BWD, HASY>(batch, filters, spatial, ds, occupancy);
+        if (!pl.ok || pl.smem > 16384) return DNB_OK;
+        static size_t smem_set = 0;
+        if (pl.smem > smem_set) {
+            DNB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem));
+            smem_set = pl.smem;
+        }
+        Workspace *ws = nullptr;
+        DNB_TRY(workspace(stream, sizeof(float4) * (size_t)pl.G * pl.P * 2, &ws));
+        fill_partition(a, pl, batch, filters, spatial, pl.P, pl.P, kSThreads);
+        constexpr int chunk = SweepKernel<BWD, A, HASY>::CHUNK;
+        a.cpu = (pl.U / 4 + chunk - 1) / chunk;
+        a.f_cpu = FastDiv((uint32_t)a.cpu);
+        a.act = act;
+        a.rec = static_cast<float4 *>(ws->scratch);
+        a.sync = ws->sync;
+        a.err = ds->error_word;
+        a.abort_flag = ds->abort_flag;
+        a.wait_ns = wait_limit_ns();
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)pl.P);
+        cfg.blockDim = dim3(kSThreads);
+        cfg.dynamicSmemBytes = pl.smem;
+        cfg.stream = stream;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeCooperative;
+        attr[0].val.cooperative = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        DNB_CUDA(cudaLaunchKernelEx(&cfg, kern, a));
+        *launched = true;
+        return after_launch(stream, what);
+    });
+}
+
+bool use_pipeline_kernel() {
+    const char *e = getenv("DNB_BN_KERNEL");
+    return e && e[0] == 'p';
+}
+
 }  // namespace
 }  // namespace dnb
 
@@ -1272,7 +1903,10 @@ dnb_status dnb_bn_act_forward_train(const float *x, float *y, float *x_norm, int
         a.rmean = rolling_mean;
         a.rvar = rolling_variance;
         bool launched = false;
-        DNB_TRY((run_persistent<false, false>(batch, filters, spatial, act, a, s, &launched, what)));
+        if (use_pipeline_kernel())
+            DNB_TRY((run_persistent<false, false>(batch, filters, spatial, act, a, s, &launched, what)));
+        else
+            DNB_TRY((run_sweep<false, false>(batch, filters, spatial, act, a, s, &launched, what)));
         if (launched) return DNB_OK;
     }
     const GGeom g = make_ggeom(batch, filters, spatial, aligned16(x));
@@ -1312,10 +1946,17 @@ dnb_status dnb_bn_act_backward(const float *x, const float *y, const float *delt
         a.mean_delta = mean_delta;
         a.var_delta = variance_delta;
         bool launched = false;
-        if (y)
-            DNB_TRY((run_persistent<true, true>(batch, filters, spatial, act, a, s, &launched, what)));
-        else
-            DNB_TRY((run_persistent<true, false>(batch, filters, spatial, act, a, s, &launched, what)));
+        if (use_pipeline_kernel()) {
+            if (y)
+                DNB_TRY((run_persistent<true, true>(batch, filters, spatial, act, a, s, &launched, what)));
+            else
+                DNB_TRY((run_persistent<true, false>(batch, filters, spatial, act, a, s, &launched, what)));
+        } else {
+            if (y)
+                DNB_TRY((run_sweep<true, true>(batch, filters, spatial, act, a, s, &launched, what)));
+            else
+                DNB_TRY((run_sweep<true, false>(batch, filters, spatial, act, a, s, &launched, what)));
+        }
         if (launched) return DNB_OK;
     }
     const GGeom g = make_ggeom(batch, filters, spatial, aligned16(x) && aligned16(delta) && (!y || aligned16(y)));

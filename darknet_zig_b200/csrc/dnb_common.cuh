@@ -53,16 +53,25 @@ struct DeviceState {
 // Scratch owned by the library for one (device, stream) pair.
 struct Workspace {
     cudaStream_t stream = nullptr;
-    // grid-barrier state: [0] = launch epoch, [1..] two banks of per-group arrival counters
+    // grid-barrier state: [0] = launch epoch, [1..] two banks of per-group arrival counters,
+    // then the sweep kernel's per-channel region (kChanStart ..)
     unsigned *sync = nullptr;
     size_t sync_words = 0;
     void *scratch = nullptr;  // per-channel partial records
     size_t scratch_bytes = 0;
 };
 
-// `sync` = 1 epoch word + 2 banks, each holding two arrays of kMaxGroups group counters.
+// `sync` = 1 epoch word + 2 banks, each holding two arrays of kMaxGroups group counters,
+// then the per-channel region of the sweep kernel: a start counter, per-channel arrival
+// counters (each reset to 0 by its last arrival) and ready tags (the launch epoch once the
+// channel's parameters are published), and the published parameters (8 floats a channel).
 constexpr int kMaxGroups = 1024;
-constexpr size_t kSyncWords = 1 + 4 * (size_t)kMaxGroups;
+constexpr int kMaxChannels = 65536;
+constexpr size_t kChanStart = (1 + 4 * (size_t)kMaxGroups + 15) & ~(size_t)15;
+constexpr size_t kChanCount = kChanStart + 16;
+constexpr size_t kChanReady = kChanCount + kMaxChannels;
+constexpr size_t kChanParams = kChanReady + kMaxChannels;
+constexpr size_t kSyncWords = kChanParams + 8 * (size_t)kMaxChannels;
 
 // The state of the current device, initialising it on first use.
 dnb_status current_device(DeviceState **out);
@@ -70,6 +79,8 @@ dnb_status current_device(DeviceState **out);
 dnb_status workspace(cudaStream_t stream, size_t scratch_bytes, Workspace **out);
 // Checks the launch that was just issued (and synchronises under sync-after-launch).
 dnb_status after_launch(cudaStream_t stream, const char *what);
+// Counts one device-side launch (kernel or memset) for dnb_launch_count; after_launch does it.
+void note_launch();
 // Spin limit for device-side waits, in nanoseconds.
 unsigned long long wait_limit_ns();
 

@@ -304,11 +304,13 @@ extern "C" dnb_status dnb_mean_noalloc(const float *x, int64_t batch, int64_t fi
         // the previous call's partials are still there: clear the slots this call reads
         DNB_CUDA(cudaMemsetAsync(partial, 0, sizeof(float) * (size_t)(filters * chunks), s));
     }
+    note_launch();
     DNB_CUDA(cudaGetLastError());
     const float scale = 1.0f / (float)(batch * spatial);  // blas.zig:107
     const unsigned warps_per_block = 8;
     const unsigned blocks = (unsigned)((filters + warps_per_block - 1) / warps_per_block);
     k_chan_close<<<blocks, 32 * warps_per_block, 0, s>>>(filters, g.chunks, partial, Close::Mean, scale, nullptr, out);
+    note_launch();
     DNB_CUDA(cudaGetLastError());
     return DNB_OK;
 }

@@ -6,6 +6,7 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <atomic>
 #include <map>
 #include <mutex>
 #include <utility>
@@ -20,6 +21,7 @@ thread_local char g_detail[512] = "";
 std::mutex g_mu;
 DeviceState g_dev[64];
 std::map<std::pair<int, cudaStream_t>, Workspace *> g_ws;
+std::atomic<unsigned long long> g_launches{0};
 bool g_sync_after_launch = false;
 unsigned long long g_wait_limit_ns = 2000ull * 1000ull * 1000ull;  // 2 s
 
@@ -104,7 +106,10 @@ dnb_status workspace(cudaStream_t stream, size_t scratch_bytes, Workspace **out)
     return DNB_OK;
 }
 
+void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
 dnb_status after_launch(cudaStream_t stream, const char *what) {
+    note_launch();
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return fail(DNB_ERR_CUDA, "launching %s failed: %s", what, cudaGetErrorString(e));
     if (g_sync_after_launch) {
@@ -187,6 +192,7 @@ dnb_status dnb_memset_zero(void *ptr, size_t bytes, dnb_stream stream) {
     if (bytes == 0) return DNB_OK;
     if (!ptr) return fail(DNB_ERR_INVALID, "ptr is null");
     DNB_CUDA(cudaMemsetAsync(ptr, 0, bytes, as_stream(stream)));
+    note_launch();
     return DNB_OK;
 }
 
@@ -236,6 +242,12 @@ dnb_status dnb_check_device_error(void) {
                 DNB_CUDA(cudaMemset(kv.second->sync, 0, kv.second->sync_words * sizeof(unsigned)));
     }
     return fail(DNB_ERR_TIMEOUT, "a device-side wait gave up (error bits 0x%x)", word[0]);
+}
+
+dnb_status dnb_launch_count(unsigned long long *count) {
+    if (!count) return fail(DNB_ERR_INVALID, "launch_count: null pointer");
+    *count = g_launches.load(std::memory_order_relaxed);
+    return DNB_OK;
 }
 
 dnb_status dnb_set_wait_limit_ms(int ms) {

@@ -56,6 +56,15 @@ def set_wait_limit_ms(ms: int) -> None:
     call("set_wait_limit_ms", int(ms))
 
 
+def launch_count() -> int:
+    """Device-side launches (kernels and memsets) the library has issued in this process."""
+    import ctypes
+
+    n = ctypes.c_ulonglong(0)
+    call("launch_count", ctypes.byref(n))
+    return int(n.value)
+
+
 def sync() -> None:
     call("sync")
 

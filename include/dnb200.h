@@ -89,6 +89,10 @@ dnb_status dnb_set_sync_after_launch(int on);
 /* Reads and clears the device-side error word of this device (set by a bounded wait that
  * gave up). Synchronises the device. Returns DNB_ERR_TIMEOUT if a wait had expired. */
 dnb_status dnb_check_device_error(void);
+/* Number of device-side launches (kernels and memsets) this library has issued in this
+ * process, all devices and threads together. No counterpart in the reference; it lets a
+ * caller check how many launches an op costs. */
+dnb_status dnb_launch_count(unsigned long long *count);
 /* Sets how long a device-side wait may spin before it gives up (default 2000 ms). */
 dnb_status dnb_set_wait_limit_ms(int ms);
 

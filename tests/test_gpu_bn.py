@@ -180,6 +180,30 @@ def test_fused_full_size_forward_backward(cuda, oracle, shape):
     test_fused_backward(cuda, oracle, shape, gpu.LEAKY, False)
 
 
+@pytest.mark.parametrize("shape", [(8, 16, 64), (2, 3, 4), (16, 40, 196), (1, 300, 100), (128, 128, 1024),
+                                   (128, 256, 784)])
+def test_fused_entries_are_one_launch(cuda, shape):
+    """With spatial % 4 == 0 and aligned tensors each fused entry is a single kernel launch
+    (the persistent kernel), not the multi-launch generic path."""
+    B, C, S = shape
+    x, gamma, beta, delta, rm0, rv0 = make_inputs(shape, seed=5)
+    y = torch.empty(x.size, dtype=torch.float32, device="cuda")
+    mean, var = torch.zeros(C, device="cuda"), torch.zeros(C, device="cuda")
+    xd, gd, bd, rm, rv = dev(x), dev(gamma), dev(beta), dev(rm0), dev(rv0)
+    n0 = gpu.launch_count()
+    gpu.bnActForwardTrain(xd, y, None, B, C, S, gd, bd, mean, var, rm, rv, gpu.LEAKY)
+    n1 = gpu.launch_count()
+    dx = torch.empty_like(y)
+    bu, su, md, vd = (torch.zeros(C, device="cuda") for _ in range(4))
+    dd = dev(delta)
+    n2 = gpu.launch_count()
+    gpu.bnActBackward(xd, None, dd, dx, B, C, S, gd, bd, mean, var, bu, su, md, vd, gpu.LEAKY)
+    n3 = gpu.launch_count()
+    torch.cuda.synchronize()
+    gpu.check_device_error()
+    assert (n1 - n0, n3 - n2) == (1, 1)
+
+
 @pytest.mark.parametrize("shape", [(8, 16, 64), (4, 17, 53), (128, 128, 1024)])
 def test_fused_is_deterministic(cuda, shape):
     B, C, S = shape
