@@ -10,8 +10,8 @@ each rank holds batch/world images.
               -> dnb_syncbn_forward_apply (Chan merge of the ranks' records, then apply)
     backward  dnb_syncbn_backward_partials -> all_reduce(SUM) of [C,2] fp64 (sum g,
               sum g*(x-mean)) -> dnb_syncbn_backward_apply
-The collectives go through a torch.distributed process group (NCCL on GPUs; the host-side
-protocol is exercised with gloo on the CPU by tests/test_syncbn_cpu.py).
+The collectives go through a torch.distributed process group (NCCL on GPUs; the same
+exchange functions run over gloo on the CPU in tests/test_syncbn_cpu.py).
 
 `combine_forward_partials` is the host restatement of the merge the device performs
 (k_fwd_finalize), used to check the protocol without a GPU.
@@ -39,6 +39,29 @@ def local_forward_partials(x: np.ndarray, batch: int, filters: int, spatial: int
     v = x.reshape(batch, filters, spatial).transpose(1, 0, 2).reshape(filters, -1).astype(np.float64)
     m = v.mean(axis=1)
     return np.stack([m, ((v - m[:, None]) ** 2).sum(axis=1)], axis=1)
+
+
+def local_backward_partials(g: np.ndarray, x: np.ndarray, mean: np.ndarray, batch: int, filters: int,
+                            spatial: int) -> np.ndarray:
+    """Host form of dnb_syncbn_backward_partials given the activation-gradient terms
+    g = delta * act'(y): [C, 2] (sum g, sum g * (x - mean)) of this shard, fp64."""
+    gv = g.reshape(batch, filters, spatial).transpose(1, 0, 2).reshape(filters, -1).astype(np.float64)
+    xv = x.reshape(batch, filters, spatial).transpose(1, 0, 2).reshape(filters, -1).astype(np.float64)
+    return np.stack([gv.sum(axis=1), (gv * (xv - np.asarray(mean, np.float64)[:, None])).sum(axis=1)], axis=1)
+
+
+def gather_forward_partials(dist, part, gathered) -> None:
+    """The forward exchange: every rank's [C, 2] fp64 (mean, M2) record into
+    gathered[world, C, 2], in rank order (so every rank merges identically)."""
+    if hasattr(dist, "all_gather_into_tensor") and part.is_cuda:
+        dist.all_gather_into_tensor(gathered, part)
+    else:
+        dist.all_gather(list(gathered.unbind(0)), part)
+
+
+def reduce_backward_partials(dist, part) -> None:
+    """The backward exchange: [C, 2] fp64 (sum g, sum g*(x-mean)) summed over ranks, in place."""
+    dist.all_reduce(part)
 
 
 class SyncBN:
@@ -74,7 +97,7 @@ class SyncBN:
         b = self._buffers(x.device)
         s = gpu._s()
         call("syncbn_forward_partials", gpu._p(x), B, C, S, b["fpart"].data_ptr(), s)
-        self.dist.all_gather_into_tensor(b["gathered"], b["fpart"])
+        gather_forward_partials(self.dist, b["fpart"], b["gathered"])
         call("syncbn_forward_apply", gpu._p(x), gpu._p(y), gpu._p(x_norm), B, C, S, b["gathered"].data_ptr(),
              self.world, gpu._p(gamma), gpu._p(beta), gpu._p(mean), gpu._p(var), gpu._p(rolling_mean),
              gpu._p(rolling_variance), int(act), s)
@@ -90,7 +113,7 @@ class SyncBN:
         s = gpu._s()
         call("syncbn_backward_partials", gpu._p(x), gpu._p(y), gpu._p(delta), B, C, S, gpu._p(gamma), gpu._p(beta),
              gpu._p(mean), gpu._p(var), int(act), b["bpart"].data_ptr(), s)
-        self.dist.all_reduce(b["bpart"])
+        reduce_backward_partials(self.dist, b["bpart"])
         call("syncbn_backward_apply", gpu._p(x), gpu._p(y), gpu._p(delta), gpu._p(dx), B, C, S, B * S * self.world,
              b["bpart"].data_ptr(), gpu._p(gamma), gpu._p(beta), gpu._p(mean), gpu._p(var), gpu._p(bias_updates),
              gpu._p(scale_updates), gpu._p(mean_delta), gpu._p(variance_delta), int(act), s)
