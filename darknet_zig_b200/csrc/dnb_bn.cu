@@ -9,22 +9,22 @@
 // forward (read x, write y) and 12 B/elem backward (read delta and x, write dx).
 //
 // The obstacle is the per-channel reduction that must finish before any element can be
-// written. The persistent kernel below keeps the second read off HBM: channels are taken
-// in groups sized to a slice of the 126 MB L2, half the CTAs stream group g+1 and reduce
-// it while the other half merge group g's partials and write its outputs, re-reading the
-// inputs from L2 (see the comment above k_bn_persistent). Every wait is bounded: a CTA
-// that gives up sets the device error word and exits; the host reports DNB_ERR_TIMEOUT.
+// written. The persistent kernel below (the sweep) keeps the second read off HBM: channels
+// are taken in groups sized to a slice of the 126 MB L2; every CTA reduces its share of a
+// group, the CTAs exchange per-channel records through global memory, and each CTA then
+// writes the outputs of its share, re-reading the inputs from L2 (see the comment above
+// k_bn_sweep). Every wait is bounded: a CTA that gives up sets the device error word and
+// exits; the host reports DNB_ERR_TIMEOUT.
 //
-// Shapes the persistent kernel does not take (spatial % 4 != 0, unaligned pointers) run
-// the generic three-launch path below, which also implements the split sync-BN entry
-// points: per-channel partials -> (caller's collective) -> finalize + apply.
+// Shapes the persistent kernel does not take (spatial % 4 != 0, unaligned pointers, more
+// than 16 channel groups) run the generic three-launch path below, which also implements
+// the split sync-BN entry points: per-channel partials -> (caller's collective) ->
+// finalize + apply.
 //
 // Per-element arithmetic follows the reference CPU code (blas.zig:137-204) operation by
 // operation without fused roundings (--fmad=false), so given the same per-channel
 // statistics the outputs are bit-identical to it.
 #include <math.h>
-
-#include <cooperative_groups.h>
 
 #include "dnb_chan.cuh"
 
@@ -421,30 +421,8 @@ dnb_status generic_bwd_apply(const GGeom &g, const float *x, const float *y, con
 }
 
 // ======================================================================================
-// persistent fused kernel: a grid-level pipeline over channel groups, TMA-staged
+// persistent fused kernel: the sweep
 // ======================================================================================
-//
-// The channels are processed in groups. One cooperative grid, two roles (even / odd CTAs,
-// so every SM runs one of each):
-//   stats CTAs  copy their balanced share of group g from HBM into shared memory with 1-D
-//               TMA bulk copies (double-buffered: group g+1 is in flight while g is
-//               reduced), reduce it per channel segment (a share spans at most two
-//               channels), publish one partial record per (CTA, segment, warp), and count
-//               themselves in stats_done[g];
-//   apply CTAs  once stats_done[g] is complete, bulk-copy the same units -- now resident in
-//               L2, where the stats copies left them -- into their own shared memory,
-//               merge the records of their share's channels (fp64, one L2 round trip,
-//               overlapping the copy), write the outputs with streaming stores from shared
-//               memory, and count themselves in apply_done[g].
-// The TMA engine keeps the bytes in flight, so neither role needs registers or warps to
-// cover HBM latency, and every input byte crosses HBM once. Stats CTAs refill a buffer
-// with group h only once apply_done[h - depth] is complete, bounding what sits in L2.
-// The only waits are a stats CTA on the apply of an earlier group and an apply CTA on the
-// stats of the group it is about to copy: no cycle. Every wait is bounded (the kernel then
-// sets the device error word, waits for its own copies, and returns).
-
-constexpr int kLThreads = 512;
-constexpr int kLWarps = kLThreads / 32;
 
 // Everything the persistent kernel needs, by value. Partition arithmetic is 32-bit with
 // FastDiv: the plan guarantees T * max(Ps, Pa) < 2^32.
@@ -452,10 +430,10 @@ struct PArgs {
     int64_t C, S;
     int N, K, U, NK;          // batch, pieces per plane, unit floats (S/K), units per channel
     int cg, G;                // channels per group, groups
-    int Ps, Pa, depth;        // stats CTAs, apply CTAs, groups resident in L2 at once (>= 3)
-    int cap_units;            // units one shared-memory buffer holds per tensor
+    int Ps, depth;            // CTAs, lag (groups whose statistics run ahead of the outputs)
+    int cap_units;            // most units a CTA's share of one group holds
     uint32_t T_full, T_last;  // units in a group (every group but the last / the last)
-    FastDiv f_u4, f_nk, f_k, f_ps, f_pa, f_tfull, f_tlast;
+    FastDiv f_nk, f_k, f_ps, f_tfull, f_tlast;
     float denom;              // batch*spatial as f32 (normalize_delta's denominator)
     float inv_denom;          // 1/denom, used only when denom is a power of two (then exact)
     int denom_pow2;
@@ -468,8 +446,7 @@ struct PArgs {
     float *bias_upd, *scale_upd, *mean_delta, *var_delta;
     int act;
     float4 *rec;              // [G][Ps][2 segments]
-    uint32_t step_q, step_r;  // kLThreads float4s = step_q units + step_r float4s
-    int cpu;                  // sweep: chunks per unit
+    int cpu;                  // chunks of 32 float4s per unit
     FastDiv f_cpu;
     unsigned *sync;           // [0] epoch, then 2 banks of {stats_done[kMaxGroups], apply_done[kMaxGroups]}
     unsigned *err, *abort_flag;
@@ -497,47 +474,6 @@ __device__ __forceinline__ Share share_of(const PArgs &a, int g, int p, const Fa
 __device__ __forceinline__ int owner_of(const PArgs &a, int g, uint32_t t, int parts) {
     const FastDiv &fd = g == a.G - 1 ? a.f_tlast : a.f_tfull;
     return (int)fd.div((t + 1) * (uint32_t)parts - 1);
-}
-
-// Element offset and segment of float4 i of a share.
-__device__ __forceinline__ void locate(const PArgs &a, const Share &sh, uint32_t i, int64_t &off, int &seg) {
-    uint32_t u, r;
-    a.f_u4.divmod(i, u, r);
-    const uint32_t t = sh.t0 + u;
-    seg = t >= sh.bnd ? 1 : 0;
-    const uint32_t cl = (uint32_t)(sh.cfirst + seg);
-    uint32_t n, k;
-    a.f_k.divmod(t - cl * (uint32_t)a.NK, n, k);
-    off = ((int64_t)n * a.C + sh.c0 + cl) * a.S + (int64_t)k * a.U + 4 * (int64_t)r;
-}
-
-// ---- TMA 1-D bulk copies and mbarriers (no multicast) ----
-__device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
-__device__ __forceinline__ void mbar_init(uint64_t *bar, unsigned count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-__device__ __forceinline__ void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
-__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, unsigned bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, unsigned parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-// global -> this CTA's shared memory, completing on `bar`
-__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, unsigned bytes, uint64_t *bar) {
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                     smem_u32(dst)),
-                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
-                 : "memory");
 }
 
 __device__ __forceinline__ float div_denom(float v, const PArgs &a) {
@@ -587,497 +523,6 @@ struct Moments {
     }
 };
 
-#ifdef DNB_PHASE_TIMING
-// Diagnostic build only (-DDNB_PHASE_TIMING): %globaltimer stamps per (CTA, group, phase):
-// stats role 0 start, 1 published; apply role 2 released, 3 merged, 4 applied.
-constexpr int kTsCtas = 1280, kTsGroups = 32, kTsPhases = 6;
-__device__ unsigned long long g_phase_ts[kTsCtas * kTsGroups * kTsPhases];
-#define DNB_STAMP(g, ph)                                                                              \
-    do {                                                                                              \
-        if (threadIdx.x == 0 && blockIdx.x < kTsCtas && (g) < kTsGroups)                              \
-            g_phase_ts[(blockIdx.x * kTsGroups + (g)) * kTsPhases + (ph)] = global_ns();              \
-    } while (0)
-#else
-#define DNB_STAMP(g, ph) \
-    do {                 \
-    } while (0)
-#endif
-
-template <bool BWD, int A, bool HASY>
-struct PipeKernel {
-    static constexpr int NT = BWD ? (HASY ? 3 : 2) : 1;  // tensors staged per unit
-
-    struct Smem {
-        float *buf;        // [2][NT][cap_units * U]
-        long long *utab;   // [2][cap_units] element offset of each staged unit
-        uint64_t *bars;    // [2]
-        float4 *wrec;      // [2 segments][kLWarps] warp partials of the stats role
-        float *ptab;       // [2 segments][8] apply records of the current group
-        int *flag;
-    };
-    __host__ __device__ static size_t buf_bytes(int cap_units, int U) {
-        return (size_t)2 * NT * cap_units * U * sizeof(float);
-    }
-    __host__ __device__ static size_t smem_bytes(int cap_units, int U) {
-        return buf_bytes(cap_units, U) + (size_t)2 * cap_units * sizeof(long long) + 2 * sizeof(uint64_t) +
-               2 * kLWarps * sizeof(float4) + 16 * sizeof(float) + 16;
-    }
-    __device__ static Smem carve(const PArgs &a, unsigned char *raw) {
-        Smem s;
-        size_t o = buf_bytes(a.cap_units, a.U);
-        s.buf = reinterpret_cast<float *>(raw);
-        s.utab = reinterpret_cast<long long *>(raw + o);
-        o += (size_t)2 * a.cap_units * sizeof(long long);
-        s.bars = reinterpret_cast<uint64_t *>(raw + o);
-        o += 2 * sizeof(uint64_t);
-        s.wrec = reinterpret_cast<float4 *>(raw + o);
-        o += 2 * kLWarps * sizeof(float4);
-        s.ptab = reinterpret_cast<float *>(raw + o);
-        o += 16 * sizeof(float);
-        s.flag = reinterpret_cast<int *>(raw + o);
-        return s;
-    }
-    __device__ static float *tbuf(const PArgs &a, const Smem &s, int b, int t) {
-        return s.buf + ((size_t)b * NT + t) * a.cap_units * a.U;
-    }
-
-    // Copies of the share (role partition `parts`) of group g into buffer b (warp 0).
-    __device__ static void issue(const PArgs &a, const Smem &s, int g, int rid, const FastDiv &parts, int b) {
-        if (threadIdx.x >= 32) return;
-        const Share sh = share_of(a, g, rid, parts);
-        const int n_units = (int)(sh.t1 - sh.t0);
-        const unsigned unit_bytes = (unsigned)a.U * sizeof(float);
-        if (threadIdx.x == 0) {
-            fence_proxy_async();  // this buffer's earlier generic-proxy reads come first
-            mbar_arrive_expect_tx(&s.bars[b], (unsigned)(n_units * NT) * unit_bytes);
-        }
-        __syncwarp();
-        const float *src[3] = {a.t0, a.t1, a.t2};
-        for (int u = threadIdx.x; u < n_units; u += 32) {
-            uint32_t cl, rem, n, k;
-            a.f_nk.divmod(sh.t0 + u, cl, rem);
-            a.f_k.divmod(rem, n, k);
-            const int64_t goff = ((int64_t)n * a.C + sh.c0 + cl) * a.S + (int64_t)k * a.U;
-            s.utab[b * a.cap_units + u] = goff;
-#pragma unroll
-            for (int tt = 0; tt < NT; ++tt)
-                bulk_g2s(tbuf(a, s, b, tt) + (size_t)u * a.U, src[tt] + goff, unit_bytes, &s.bars[b]);
-        }
-    }
-
-    // Bounded wait for buffer b's copies (phase parity); every thread calls it.
-    __device__ static bool wait_copies(const PArgs &a, const Smem &s, int b, unsigned parity) {
-        const unsigned long long deadline = global_ns() + a.wait_ns;
-        unsigned it = 0;
-        while (!mbar_try_wait(&s.bars[b], parity)) {
-            if ((++it & 63u) == 0 && global_ns() > deadline) {
-                atomicOr(a.err, DEVERR_WAIT_COPY);
-                atomicExch(a.abort_flag, 1u);
-                return false;
-            }
-        }
-        return true;
-    }
-
-    __device__ static BwdParam fwd_params_of(const PArgs &a, int64_t c) {
-        BwdParam p;
-        p.m = a.mean_in[c];
-        p.inv = 1.0f / (sqrtf(a.var_in[c]) + 0.000001f);
-        p.g = a.scales[c];
-        p.b = a.biases[c];
-        return p;
-    }
-
-    // stats role: records of CTA `rid`'s share of group g, staged in buffer b
-    __device__ static void stats(const PArgs &a, const Smem &s, int g, int rid, int b) {
-        const Share sh = share_of(a, g, rid, a.f_ps);
-        if (sh.nseg == 0) return;
-        const uint32_t u4 = (uint32_t)a.U >> 2;
-        const uint32_t n4 = (sh.t1 - sh.t0) * u4;
-        const uint32_t i_bnd = ((sh.t1 < sh.bnd ? sh.t1 : sh.bnd) - sh.t0) * u4;  // first float4 of segment 1
-        const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-        const float4 *b0 = reinterpret_cast<const float4 *>(tbuf(a, s, b, 0));
-        float4 rec[2];
-        if constexpr (!BWD) {
-            Moments mo[2];
-#pragma unroll 4
-            for (uint32_t i = threadIdx.x; i < n4; i += kLThreads) {
-                const float4 v = b0[i];
-                if (i < i_bnd) mo[0].add4(v);
-                else mo[1].add4(v);
-            }
-            rec[0] = mo[0].warp_summary();
-            rec[1] = mo[1].warp_summary();
-        } else {
-            const float4 *bx = reinterpret_cast<const float4 *>(tbuf(a, s, b, 1));
-            const float4 *by = reinterpret_cast<const float4 *>(tbuf(a, s, b, NT - 1));
-            const BwdParam p0 = fwd_params_of(a, (int64_t)sh.c0 + sh.cfirst);
-            const BwdParam p1 = sh.nseg > 1 ? fwd_params_of(a, (int64_t)sh.c0 + sh.cfirst + 1) : p0;
-            float s1[2] = {0.0f, 0.0f}, s2[2] = {0.0f, 0.0f};
-#pragma unroll 2
-            for (uint32_t i = threadIdx.x; i < n4; i += kLThreads) {
-                const int sg = i < i_bnd ? 0 : 1;
-                const BwdParam &p = sg ? p1 : p0;
-                const float4 d = b0[i], xv = bx[i];
-                const float4 yy = HASY ? by[i] : xv;
-                const float g0 = bn_grad1<A, HASY>(d.x, xv.x, yy.x, p, a.act);
-                const float g1 = bn_grad1<A, HASY>(d.y, xv.y, yy.y, p, a.act);
-                const float g2 = bn_grad1<A, HASY>(d.z, xv.z, yy.z, p, a.act);
-                const float g3 = bn_grad1<A, HASY>(d.w, xv.w, yy.w, p, a.act);
-                const float t1 = (g0 + g1) + (g2 + g3);
-                const float t2 = (g0 * (xv.x - p.m) + g1 * (xv.y - p.m)) + (g2 * (xv.z - p.m) + g3 * (xv.w - p.m));
-                if (sg) {
-                    s1[1] += t1;
-                    s2[1] += t2;
-                } else {
-                    s1[0] += t1;
-                    s2[0] += t2;
-                }
-            }
-            rec[0] = make_float4(warp_sum(s1[0]), warp_sum(s2[0]), 0.0f, 0.0f);
-            rec[1] = make_float4(warp_sum(s1[1]), warp_sum(s2[1]), 0.0f, 0.0f);
-        }
-        // one record per (CTA, segment): warp 0 combines the warps' partials
-        if (lane == 0) {
-            s.wrec[warp] = rec[0];
-            s.wrec[kLWarps + warp] = rec[1];
-        }
-        __syncthreads();
-        if (warp == 0) {
-            for (int j = 0; j < sh.nseg; ++j) {
-                float4 r = lane < kLWarps ? s.wrec[j * kLWarps + lane] : make_float4(0, 0, 0, 0);
-                if constexpr (!BWD) {
-#pragma unroll
-                    for (int o = kLWarps / 2; o > 0; o >>= 1) {
-                        const float cb = __shfl_xor_sync(0xffffffffu, r.x, o);
-                        const float mb = __shfl_xor_sync(0xffffffffu, r.y, o);
-                        const float qb = __shfl_xor_sync(0xffffffffu, r.z, o);
-                        chan_merge(r.x, r.y, r.z, cb, mb, qb);
-                    }
-                } else {
-#pragma unroll
-                    for (int o = kLWarps / 2; o > 0; o >>= 1) {
-                        r.x += __shfl_xor_sync(0xffffffffu, r.x, o);
-                        r.y += __shfl_xor_sync(0xffffffffu, r.y, o);
-                    }
-                }
-                if (lane == 0) a.rec[((int64_t)g * a.Ps + rid) * 2 + j] = r;
-            }
-        }
-    }
-
-    // One release-add per CTA on counter[g] after the whole CTA's work (CTA barrier, then
-    // a GPU-scope fence by thread 0, as a grid barrier publishes a CTA's writes).
-    __device__ static void arrive(unsigned *counter, int g) {
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            __threadfence();
-            asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(counter + g) : "memory");
-        }
-    }
-
-    // Wait (bounded) until counter[g] reaches `target`; block-uniform result.
-    __device__ static bool wait_for(const PArgs &a, int *flag, const unsigned *counter, int g, unsigned target) {
-        if (threadIdx.x == 0) {
-            int ok = 1;
-            if (ld_acquire_gpu(&counter[g]) < target) {
-                const unsigned long long deadline = global_ns() + a.wait_ns;
-                while (ld_acquire_gpu(&counter[g]) < target) {
-                    if (ld_volatile(a.abort_flag)) {
-                        ok = 0;
-                        break;
-                    }
-                    if (global_ns() > deadline) {
-                        atomicOr(a.err, DEVERR_WAIT_BARRIER);
-                        atomicExch(a.abort_flag, 1u);
-                        ok = 0;
-                        break;
-                    }
-                    __nanosleep(64);
-                }
-            }
-            *flag = ok;
-        }
-        __syncthreads();
-        return *flag != 0;
-    }
-
-    // Non-blocking: has counter[g] reached `target`? Block-uniform.
-    __device__ static bool ready(int *flag, const unsigned *counter, int g, unsigned target) {
-        if (threadIdx.x == 0) *flag = ld_acquire_gpu(&counter[g]) >= target;
-        __syncthreads();
-        return *flag != 0;
-    }
-
-    // apply role: merge the records of the (at most two) channels of CTA `rid`'s share.
-    // Records of stats CTAs between the first and last owner that hold no unit of the
-    // channel (a group with fewer units than CTAs) are skipped.
-    __device__ static void merge(const PArgs &a, float *ptab, int g, int rid) {
-        const Share sh = share_of(a, g, rid, a.f_pa);
-        const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-        if (warp < sh.nseg) {
-            const int cl = sh.cfirst + warp;
-            const int64_t c = (int64_t)sh.c0 + cl;
-            // per-channel inputs are requested before the records so the loads overlap
-            float gamma = 0.0f, beta = 0.0f, m_in = 0.0f, v_in = 0.0f, rm = 0.0f, rv = 0.0f;
-            const uint32_t ua = (uint32_t)cl * a.NK, ub = ua + a.NK;
-            // the apply CTA owning the channel's first unit writes the per-channel outputs
-            const bool write = owner_of(a, g, ua, a.Pa) == rid;
-            if (lane == 0) {
-                gamma = a.scales[c];
-                beta = a.biases[c];
-                if constexpr (BWD) {
-                    m_in = a.mean_in[c];
-                    v_in = a.var_in[c];
-                } else if (write) {
-                    rm = a.rmean[c];
-                    rv = a.rvar[c];
-                }
-            }
-            const int plo = owner_of(a, g, ua, a.Ps), phi = owner_of(a, g, ub - 1, a.Ps);
-            const int nrec = phi - plo + 1;
-            float *out = ptab + warp * 8;
-            constexpr int R = 2;  // records held per lane: one L2 round trip up to 64 records
-            float4 r[R];
-            bool have[R];
-            auto load = [&](int idx, float4 &dst) -> bool {
-                const int p = plo + idx;
-                const Share o = share_of(a, g, p, a.f_ps);
-                const uint32_t lo = ua > o.t0 ? ua : o.t0, hi = ub < o.t1 ? ub : o.t1;
-                if (hi <= lo) return false;
-                dst = __ldcg(&a.rec[((int64_t)g * a.Ps + p) * 2 + (cl - o.cfirst)]);
-                return true;
-            };
-#pragma unroll
-            for (int k = 0; k < R; ++k) {
-                const int idx = lane + 32 * k;
-                have[k] = idx < nrec && load(idx, r[k]);
-            }
-            if constexpr (!BWD) {
-                double sn = 0.0, smn = 0.0;
-#pragma unroll
-                for (int k = 0; k < R; ++k)
-                    if (have[k]) {
-                        sn += (double)r[k].x;
-                        smn += (double)r[k].x * (double)r[k].y;
-                    }
-                for (int idx = lane + 32 * R; idx < nrec; idx += 32) {
-                    float4 t;
-                    if (!load(idx, t)) continue;
-                    sn += (double)t.x;
-                    smn += (double)t.x * (double)t.y;
-                }
-                sn = warp_sum(sn);
-                const double mu = warp_sum(smn) / sn;
-                double m2 = 0.0;
-#pragma unroll
-                for (int k = 0; k < R; ++k)
-                    if (have[k]) {
-                        const double d = (double)r[k].y - mu;
-                        m2 += (double)r[k].z + (double)r[k].x * d * d;
-                    }
-                for (int idx = lane + 32 * R; idx < nrec; idx += 32) {
-                    float4 t;
-                    if (!load(idx, t)) continue;
-                    const double d = (double)t.y - mu;
-                    m2 += (double)t.z + (double)t.x * d * d;
-                }
-                m2 = warp_sum(m2);
-                if (lane == 0) {
-                    const FwdClose f = fwd_close(mu, m2, sn);
-                    if (write) {
-                        a.mean[c] = f.m;
-                        a.var[c] = f.var;
-                        a.rmean[c] = rolling(rm, f.m);
-                        a.rvar[c] = rolling(rv, f.var);
-                    }
-                    out[0] = f.m;
-                    out[1] = f.inv;
-                    out[2] = gamma;
-                    out[3] = beta;
-                }
-            } else {
-                double s1 = 0.0, s2 = 0.0;
-#pragma unroll
-                for (int k = 0; k < R; ++k)
-                    if (have[k]) {
-                        s1 += (double)r[k].x;
-                        s2 += (double)r[k].y;
-                    }
-                for (int idx = lane + 32 * R; idx < nrec; idx += 32) {
-                    float4 t;
-                    if (!load(idx, t)) continue;
-                    s1 += (double)t.x;
-                    s2 += (double)t.y;
-                }
-                s1 = warp_sum(s1);
-                s2 = warp_sum(s2);
-                if (lane == 0) {
-                    const BwdParam bp = bwd_close(s1, s2, m_in, v_in, gamma, beta, a.denom, a.bias_upd, a.scale_upd,
-                                                  a.mean_delta, a.var_delta, c, write);
-                    *reinterpret_cast<BwdParam *>(out) = bp;
-                }
-            }
-        }
-        __syncthreads();
-    }
-
-    // apply role: outputs of CTA `rid`'s share of group g from buffer b. Thread i walks the
-    // share's float4s i, i + kLThreads, ... tracking (unit, float4 within unit) by
-    // increments; a unit's element offset comes from the table written at copy time.
-    __device__ static void apply(const PArgs &a, const Smem &s, int g, int rid, int b) {
-        const Share sh = share_of(a, g, rid, a.f_pa);
-        if (sh.nseg == 0) return;
-        const uint32_t u4 = (uint32_t)a.U >> 2;
-        const uint32_t n4 = (sh.t1 - sh.t0) * u4;
-        const uint32_t i_bnd = ((sh.t1 < sh.bnd ? sh.t1 : sh.bnd) - sh.t0) * u4;
-        const long long *ut = s.utab + b * a.cap_units;
-        const float4 *b0 = reinterpret_cast<const float4 *>(tbuf(a, s, b, 0));
-        uint32_t u, r;
-        a.f_u4.divmod(threadIdx.x, u, r);
-        if constexpr (!BWD) {
-            const float4 q0 = *reinterpret_cast<const float4 *>(s.ptab);
-            const float4 q1 = *reinterpret_cast<const float4 *>(s.ptab + 8);
-#pragma unroll 4
-            for (uint32_t i = threadIdx.x; i < n4; i += kLThreads) {
-                const int64_t off = ut[u] + 4 * (int64_t)r;
-                const float4 v = b0[i];
-                const float4 p = i < i_bnd ? q0 : q1;
-                if (a.xnorm)
-                    st4_stream(a.xnorm + off, make_float4((v.x - p.x) * p.y, (v.y - p.x) * p.y, (v.z - p.x) * p.y,
-                                                          (v.w - p.x) * p.y));
-                st4_stream(a.out + off, make_float4(bn_fwd1<A>(v.x, p.x, p.y, p.z, p.w, a.act),
-                                                    bn_fwd1<A>(v.y, p.x, p.y, p.z, p.w, a.act),
-                                                    bn_fwd1<A>(v.z, p.x, p.y, p.z, p.w, a.act),
-                                                    bn_fwd1<A>(v.w, p.x, p.y, p.z, p.w, a.act)));
-                u += a.step_q;
-                r += a.step_r;
-                if (r >= u4) {
-                    r -= u4;
-                    ++u;
-                }
-            }
-        } else {
-            const float4 *bx = reinterpret_cast<const float4 *>(tbuf(a, s, b, 1));
-            const float4 *by = reinterpret_cast<const float4 *>(tbuf(a, s, b, NT - 1));
-            const BwdParam q0 = *reinterpret_cast<const BwdParam *>(s.ptab);
-            const BwdParam q1 = *reinterpret_cast<const BwdParam *>(s.ptab + 8);
-#pragma unroll 2
-            for (uint32_t i = threadIdx.x; i < n4; i += kLThreads) {
-                const int64_t off = ut[u] + 4 * (int64_t)r;
-                const BwdParam &p = i < i_bnd ? q0 : q1;
-                const float4 d = b0[i], xv = bx[i];
-                const float4 yy = HASY ? by[i] : xv;
-                st4_stream(a.out + off,
-                           make_float4(bn_dx_p(bn_grad1<A, HASY>(d.x, xv.x, yy.x, p, a.act), xv.x, p, a),
-                                       bn_dx_p(bn_grad1<A, HASY>(d.y, xv.y, yy.y, p, a.act), xv.y, p, a),
-                                       bn_dx_p(bn_grad1<A, HASY>(d.z, xv.z, yy.z, p, a.act), xv.z, p, a),
-                                       bn_dx_p(bn_grad1<A, HASY>(d.w, xv.w, yy.w, p, a.act), xv.w, p, a)));
-                u += a.step_q;
-                r += a.step_r;
-                if (r >= u4) {
-                    r -= u4;
-                    ++u;
-                }
-            }
-        }
-    }
-};
-
-template <bool BWD, int A, bool HASY>
-__global__ void __launch_bounds__(kLThreads, 2) k_bn_persistent(PArgs a) {
-    using K = PipeKernel<BWD, A, HASY>;
-    extern __shared__ __align__(128) unsigned char smem_raw[];
-    const typename K::Smem s = K::carve(a, smem_raw);
-    __shared__ unsigned s_epoch;
-
-    if (threadIdx.x == 0) {
-        s_epoch = ld_volatile(&a.sync[0]);
-        mbar_init(&s.bars[0], 1);
-        mbar_init(&s.bars[1], 1);
-        fence_mbar_init();
-    }
-    __syncthreads();
-    const unsigned epoch = s_epoch;
-    unsigned *stats_done = a.sync + 1 + (size_t)(epoch & 1u) * 2 * kMaxGroups;
-    unsigned *apply_done = stats_done + kMaxGroups;
-    const bool stats_role = (blockIdx.x & 1u) == 0;
-    const int rid = (int)(blockIdx.x >> 1);
-    // pending[b] = parity of the copy outstanding on buffer b, or -1
-    int pending[2] = {-1, -1};
-    unsigned uses[2] = {0, 0};
-    auto issue = [&](int g, const FastDiv &parts, int b) {
-        K::issue(a, s, g, rid, parts, b);
-        pending[b] = (int)(uses[b] & 1u);
-        ++uses[b];
-    };
-    bool ok = true;
-
-    if (stats_role) {
-        if (rid == 0) {  // the next launch's bank
-            unsigned *other = a.sync + 1 + (size_t)((epoch & 1u) ^ 1u) * 2 * kMaxGroups;
-            for (int i = threadIdx.x; i < 2 * kMaxGroups; i += kLThreads) other[i] = 0u;
-        }
-        issue(0, a.f_ps, 0);
-        if (a.G > 1) issue(1, a.f_ps, 1);
-        for (int g = 0; g < a.G; ++g) {
-            const int b = g & 1;
-            // every wait result is made block-uniform before it steers control flow
-            ok = __syncthreads_and(K::wait_copies(a, s, b, (unsigned)pending[b])) != 0;
-            if (!ok) break;
-            DNB_STAMP(g, 0);
-            K::stats(a, s, g, rid, b);
-            pending[b] = -1;
-            K::arrive(stats_done, g);  // its barrier also ends every read of buffer b
-            DNB_STAMP(g, 1);
-            const int h = g + 2;
-            if (h < a.G) {
-                if (h >= a.depth && !K::wait_for(a, s.flag, apply_done, h - a.depth, (unsigned)a.Pa)) {
-                    ok = false;
-                    break;
-                }
-                issue(h, a.f_ps, b);
-            }
-        }
-        // every CTA has read the epoch once every apply CTA has counted itself in the last
-        // group: advance it for the next launch
-        if (rid == 0 && ok && K::wait_for(a, s.flag, apply_done, a.G - 1, (unsigned)a.Pa) && threadIdx.x == 0)
-            atomicExch(&a.sync[0], epoch + 1);
-    } else {
-        bool next_issued = false;
-        ok = K::wait_for(a, s.flag, stats_done, 0, (unsigned)a.Ps);
-        if (ok) issue(0, a.f_pa, 0);
-        for (int g = 0; ok && g < a.G; ++g) {
-            const int b = g & 1;
-            // start the copy of group g+1 now if its stats are already complete
-            next_issued = false;
-            if (g + 1 < a.G && K::ready(s.flag, stats_done, g + 1, (unsigned)a.Ps)) {
-                issue(g + 1, a.f_pa, b ^ 1);
-                next_issued = true;
-            }
-            DNB_STAMP(g, 2);
-            K::merge(a, s.ptab, g, rid);
-            DNB_STAMP(g, 3);
-            ok = __syncthreads_and(K::wait_copies(a, s, b, (unsigned)pending[b])) != 0;
-            if (!ok) break;
-            K::apply(a, s, g, rid, b);
-            pending[b] = -1;
-            K::arrive(apply_done, g);
-            DNB_STAMP(g, 4);
-            if (g + 1 < a.G && !next_issued) {
-                ok = K::wait_for(a, s.flag, stats_done, g + 1, (unsigned)a.Ps);
-                if (!ok) break;
-                issue(g + 1, a.f_pa, b ^ 1);
-            }
-        }
-    }
-    if (!ok) {
-        // leave no copy in flight into this CTA's shared memory
-        for (int b = 0; b < 2; ++b)
-            if (pending[b] >= 0) K::wait_copies(a, s, b, (unsigned)pending[b]);
-    }
-}
-
 struct PPlan {
     bool ok = false;
     int K, U, cg, G, P, depth, cap_units, ctas_per_sm;
@@ -1090,167 +535,26 @@ int env_int(const char *name, int dflt, int lo, int hi) {
     return v < lo ? lo : (v > hi ? hi : v);
 }
 
-// One CTA of each role per SM by default (DNB_BN_CTAS_PER_SM, even); each CTA double-buffers
-// its share of a group in shared memory, so a group holds at most
-// cap_units * (CTAs per role) units; DNB_BN_GROUP_MB (default: as large as that allows)
-// can make groups smaller. Units are U = spatial/K floats, K the smallest divisor for which
-// a unit fits a buffer and every CTA gets >= 4 units; cg stays <= CTAs per role so a share
-// spans at most two channels.
-template <bool BWD, bool HASY>
-PPlan plan_persistent(int64_t batch, int64_t filters, int64_t spatial, const DeviceState *ds, int occupancy) {
-    using K = PipeKernel<BWD, DNB_ACT_LEAKY, HASY>;
-    constexpr int nt = K::NT;
-    PPlan pl;
-    if (spatial % 4 != 0 || batch <= 0 || filters <= 0) return pl;
-    int ctas = env_int("DNB_BN_CTAS_PER_SM", 2, 2, 8) & ~1;
-    if (ctas > occupancy) ctas = occupancy & ~1;
-    if (ctas < 2) return pl;
-    size_t per_cta = (size_t)ds->smem_per_sm / ctas - (size_t)ds->smem_reserved - 256;  // 256: static smem
-    if (per_cta > (size_t)ds->max_smem_optin) per_cta = (size_t)ds->max_smem_optin;
-    const size_t per_buf = (per_cta - 512) / (2 * nt);  // one buffer, one tensor
-    const int64_t P = (int64_t)ds->sm_count * ctas, half = P / 2;
-    int64_t k = 0;
-    for (int64_t kk = 1; kk <= spatial; ++kk) {
-        if (spatial % kk || (spatial / kk) % 4 || (size_t)(spatial / kk) * 4 > per_buf) continue;
-        if (k == 0) k = kk;
-        if (filters * batch * kk >= 4 * half || spatial / kk <= 64) {
-            k = kk;
-            break;
-        }
-    }
-    if (k == 0) return pl;
-    const int64_t U = spatial / k, NK = batch * k;
-    const int64_t cap = (int64_t)(per_buf / ((size_t)U * 4));
-    int64_t cg = cap * half / NK;
-    const int group_mb = env_int("DNB_BN_GROUP_MB", 0, 0, 4096);
-    if (group_mb > 0) {
-        const int64_t want = ((int64_t)group_mb << 20) / (batch * spatial * 4 * nt);
-        if (want < cg) cg = want;
-    }
-    if (cg > half) cg = half;
-    if (cg > filters) cg = filters;
-    if (cg < 1) return pl;
-    int64_t G = (filters + cg - 1) / cg;
-    cg = (filters + G - 1) / G;
-    G = (filters + cg - 1) / cg;
-    if (G > kMaxGroups) return pl;
-    const int64_t T = cg * NK;
-    const int64_t share = (T + half - 1) / half;
-    if (share > cap || (uint64_t)T * (uint64_t)half >= (1ull << 32) - (uint64_t)half) return pl;
-    pl.K = (int)k;
-    pl.U = (int)U;
-    pl.cg = (int)cg;
-    pl.G = (int)G;
-    pl.P = (int)P;
-    pl.depth = env_int("DNB_BN_DEPTH", 4, 3, 16);
-    pl.cap_units = (int)share;  // buffers only as large as a share
-    pl.ctas_per_sm = ctas;
-    pl.smem = K::smem_bytes(pl.cap_units, pl.U);
-    pl.ok = pl.smem <= per_cta;
-    return pl;
-}
-
 bool persistent_disabled() {
     const char *e = getenv("DNB_BN_PERSISTENT");
     return e && e[0] == '0';
 }
 
-// Plans and launches the persistent kernel for `a` (tensor and parameter pointers already
-// set). *launched stays false when the shape is not one the kernel takes.
-template <bool BWD, bool HASY>
-dnb_status run_persistent(int64_t batch, int64_t filters, int64_t spatial, int act, PArgs a, cudaStream_t stream,
-                          bool *launched, const char *what) {
-    *launched = false;
-    DeviceState *ds = nullptr;
-    DNB_TRY(current_device(&ds));
-    return dispatch_act(act, [&]<int A>() -> dnb_status {
-        auto kern = k_bn_persistent<BWD, A, HASY>;
-        // CTAs of this instantiation one SM holds by registers and threads (shared memory
-        // is sized by the plan)
-        static int reg_occupancy = -1;
-        if (reg_occupancy < 0) {
-            cudaFuncAttributes fa;
-            DNB_CUDA(cudaFuncGetAttributes(&fa, kern));
-            const int regs = fa.numRegs > 0 ? fa.numRegs : 1;
-            reg_occupancy = 65536 / (regs * kLThreads);
-        }
-        const PPlan pl = plan_persistent<BWD, HASY>(batch, filters, spatial, ds, reg_occupancy);
-        if (!pl.ok) return DNB_OK;
-        static size_t smem_set = 0;
-        if (pl.smem > smem_set) {
-            DNB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem));
-            smem_set = pl.smem;
-        }
-        const int half = pl.P / 2;
-        Workspace *ws = nullptr;
-        DNB_TRY(workspace(stream, sizeof(float4) * (size_t)pl.G * half * 2, &ws));
-        a.C = filters;
-        a.S = spatial;
-        a.N = (int)batch;
-        a.K = pl.K;
-        a.U = pl.U;
-        a.NK = (int)(batch * pl.K);
-        a.cg = pl.cg;
-        a.G = pl.G;
-        a.Ps = half;
-        a.Pa = half;
-        a.depth = pl.depth;
-        a.cap_units = pl.cap_units;
-        a.T_full = (uint32_t)pl.cg * (uint32_t)a.NK;
-        a.T_last = (uint32_t)(filters - (int64_t)(pl.G - 1) * pl.cg) * (uint32_t)a.NK;
-        a.f_u4 = FastDiv((uint32_t)(pl.U / 4));
-        a.step_q = (uint32_t)(kLThreads / (pl.U / 4));
-        a.step_r = (uint32_t)(kLThreads % (pl.U / 4));
-        a.f_nk = FastDiv((uint32_t)a.NK);
-        a.f_k = FastDiv((uint32_t)pl.K);
-        a.f_ps = FastDiv((uint32_t)half);
-        a.f_pa = FastDiv((uint32_t)half);
-        a.f_tfull = FastDiv(a.T_full);
-        a.f_tlast = FastDiv(a.T_last);
-        a.denom = (float)(spatial * batch);
-        // dividing by a power of two equals multiplying by its exact reciprocal
-        int e2 = 0;
-        a.denom_pow2 = frexpf(a.denom, &e2) == 0.5f;
-        a.inv_denom = 1.0f / a.denom;
-        a.act = act;
-        a.rec = static_cast<float4 *>(ws->scratch);
-        a.sync = ws->sync;
-        a.err = ds->error_word;
-        a.abort_flag = ds->abort_flag;
-        a.wait_ns = wait_limit_ns();
-        // every CTA must be resident: a cooperative launch
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3((unsigned)pl.P);
-        cfg.blockDim = dim3(kLThreads);
-        cfg.dynamicSmemBytes = pl.smem;
-        cfg.stream = stream;
-        cudaLaunchAttribute attr[1];
-        attr[0].id = cudaLaunchAttributeCooperative;
-        attr[0].val.cooperative = 1;
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
-        DNB_CUDA(cudaLaunchKernelEx(&cfg, kern, a));
-        *launched = true;
-        return after_launch(stream, what);
-    });
-}
-
-// ======================================================================================
-// persistent fused kernel, single role: the sweep
-// ======================================================================================
-//
 // Every CTA owns the same balanced share of each channel group in both passes, and its
-// warps are split in two. The 15 streaming warps reduce group g+1 (HBM reads) and then
-// write group g's outputs (its share re-read from L2); they never touch global
-// synchronisation. The control warp takes group g's per-warp partials from shared memory,
-// publishes the CTA's records, counts the CTA in stats_done[g], waits until every CTA has
-// done so, merges the records of the share's channels and hands the apply parameters back
-// through shared memory -- all while the streaming warps reduce group g+1, so the latency
-// of the grid-wide exchange (several L2 round trips behind saturated memory pipes) stays
-// off the streaming path. Statistics loads carry an L2 evict_last policy, output-pass loads
-// and stores evict_first, so a group stays in L2 between its two passes; groups are sized
-// so that two fit in L2. Every global wait is bounded; on timeout the control warp sets
-// the device error word and tells the streaming warps to stop.
+// warps are split in two. The 15 streaming warps reduce the groups (HBM reads) and write
+// the outputs of each group once its parameters are known (the share re-read from L2),
+// running `lag` groups of statistics ahead of the outputs; each warp walks its own chunks
+// and meets the others only through shared-memory counters, so one warp's phase change
+// never drains the whole CTA. The control warp polls two things: a group whose per-warp
+// partials are all in (it publishes the CTA's records and counts the CTA in
+// stats_done[g]), and the oldest published group that every CTA has counted itself in (it
+// merges the records of the share's channels and hands the apply parameters back through
+// shared memory). Publishing never waits behind a merge, so the exchanges of consecutive
+// groups overlap, and the grid-wide exchange (several L2 round trips behind saturated
+// memory pipes) stays off the streaming path. Statistics loads carry an L2 evict_last
+// policy, output-pass loads and stores evict_first, so a group stays in L2 between its two
+// passes. Every wait is bounded; on timeout the control warp sets the device error word
+// and tells the streaming warps to stop.
 
 constexpr int kSThreads = 512;              // threads of a sweep CTA
 constexpr int kSMinBlocks = 2;              // CTAs per SM the register budget is set for
@@ -1278,69 +582,90 @@ __device__ __forceinline__ void st4_hint(float *p, float4 v, uint64_t pol) {
                  "f"(v.y), "f"(v.z), "f"(v.w), "l"(pol)
                  : "memory");
 }
-// Named CTA barriers: bar_sync waits for `count` threads, bar_arrive counts without waiting.
-// The non-aligned forms count threads one by one, so a warp whose lanes reach the barrier
-// apart (after lane-dependent code) is still counted once per thread; the __syncwarp
-// brings the lanes together first anyway.
-__device__ __forceinline__ void bar_sync(int id, int count) {
-    __syncwarp();
-    asm volatile("barrier.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
-}
-__device__ __forceinline__ void bar_arrive(int id, int count) {
-    __syncwarp();
-    asm volatile("barrier.arrive %0, %1;" ::"r"(id), "r"(count) : "memory");
-}
-// barrier ids: 1,2 = stats of group g done (g & 1); 3,4 = parameters of group g ready;
-// 5 = the streaming warps among themselves
-constexpr int kBarStats = 1, kBarParams = 3, kBarStream = 5;
-constexpr int kStreamThreads = kSWarps * 32;
+constexpr int kMaxSweepGroups = 16;
 
 template <bool BWD, int A, bool HASY>
 struct SweepKernel {
-    using PK = PipeKernel<BWD, A, HASY>;
     static constexpr int UNROLL = BWD ? 2 : 4;  // float4s per tensor in flight per thread
     static constexpr int CHUNK = 32 * UNROLL;   // float4s of one unit a warp takes at a time
 
+    // Per-group state, one buffer per group (G <= kMaxSweepGroups).
     struct Smem {
-        uint32_t *utab;  // [2][cap_units] element offset of each unit of the share (< 2^32)
-        float4 *wrec;    // [2 buffers][2 segments][kSWarps] per-warp partials
-        float *ptab;     // [2 buffers][2 segments][8] apply parameters
-        float4 *stab;    // [2 buffers][2 segments] forward parameters for the backward's stats
+        uint32_t *utab;  // [G][cap_units] element offset of each unit of the share (< 2^32)
+        float4 *wrec;    // [G][2 segments][kSWarps] per-warp partials
+        float *ptab;     // [G][2 segments][8] apply parameters
+        float4 *stab;    // [G][2 segments] forward parameters for the backward's stats
+        int *done;       // [G] streaming warps that have left their partials of group g
+        int *ready;      // [G] 1 once the parameters of group g are in ptab
         int *stop;       // set by the control warp when a wait gave up
     };
-    __host__ __device__ static size_t smem_bytes(int cap_units) {
-        return (((size_t)2 * cap_units * sizeof(uint32_t) + 15) & ~(size_t)15) + 4 * kSWarps * sizeof(float4) +
-               32 * sizeof(float) + 4 * sizeof(float4) + 16;
+    __host__ __device__ static size_t smem_bytes(int cap_units, int groups) {
+        return (((size_t)groups * cap_units * sizeof(uint32_t) + 15) & ~(size_t)15) +
+               (size_t)groups * (2 * kSWarps * sizeof(float4) + 16 * sizeof(float) + 2 * sizeof(float4) +
+                                 2 * sizeof(int)) +
+               16;
     }
     __device__ static Smem carve(const PArgs &a, unsigned char *raw) {
+        const int G = a.G;
         Smem s;
         size_t o = 0;
         s.utab = reinterpret_cast<uint32_t *>(raw);
-        o += ((size_t)2 * a.cap_units * sizeof(uint32_t) + 15) & ~(size_t)15;
+        o += ((size_t)G * a.cap_units * sizeof(uint32_t) + 15) & ~(size_t)15;
         s.wrec = reinterpret_cast<float4 *>(raw + o);
-        o += 4 * kSWarps * sizeof(float4);
-        s.ptab = reinterpret_cast<float *>(raw + o);
-        o += 32 * sizeof(float);
+        o += (size_t)G * 2 * kSWarps * sizeof(float4);
         s.stab = reinterpret_cast<float4 *>(raw + o);
-        o += 4 * sizeof(float4);
+        o += (size_t)G * 2 * sizeof(float4);
+        s.ptab = reinterpret_cast<float *>(raw + o);
+        o += (size_t)G * 16 * sizeof(float);
+        s.done = reinterpret_cast<int *>(raw + o);
+        o += (size_t)G * sizeof(int);
+        s.ready = reinterpret_cast<int *>(raw + o);
+        o += (size_t)G * sizeof(int);
         s.stop = reinterpret_cast<int *>(raw + o);
         return s;
     }
 
-    // streaming warps: element offsets of the units of CTA rid's share of group g into
-    // table b (and, for the backward, the forward parameters of its segments)
+    // Bounded spin of a whole warp until *flag >= want; false if the control warp stopped
+    // the CTA or the wait gave up (the latter sets the device error word).
+    __device__ static bool wait_smem(const PArgs &a, const Smem &s, const int *flag, int want) {
+        const volatile int *f = flag;
+        const volatile int *stop = s.stop;
+        if (*f >= want) {
+            __threadfence_block();
+            return true;
+        }
+        const unsigned long long deadline = global_ns() + a.wait_ns;
+        while (*f < want) {
+            if (*stop) return false;
+            if (global_ns() > deadline) {
+                if ((threadIdx.x & 31) == 0) {
+                    atomicOr(a.err, DEVERR_WAIT_BARRIER);
+                    atomicExch(a.abort_flag, 1u);
+                }
+                return false;
+            }
+            __nanosleep(32);
+        }
+        __threadfence_block();
+        return true;
+    }
+
+    // every thread: element offsets of the units of CTA rid's share of group g into table b
+    // (and, for the backward, the forward parameters of its segments)
     __device__ static void tabulate(const PArgs &a, const Smem &s, int g, int rid, int b) {
         const Share sh = share_of(a, g, rid, a.f_ps);
         const int n_units = (int)(sh.t1 - sh.t0);
-        for (int u = threadIdx.x; u < n_units; u += kStreamThreads) {
+        for (int u = threadIdx.x; u < n_units; u += kSThreads) {
             uint32_t cl, rem, n, k;
             a.f_nk.divmod(sh.t0 + u, cl, rem);
             a.f_k.divmod(rem, n, k);
             s.utab[b * a.cap_units + u] = (uint32_t)(((int64_t)n * a.C + sh.c0 + cl) * a.S + (int64_t)k * a.U);
         }
         if (BWD && threadIdx.x < sh.nseg) {
-            const BwdParam p = PK::fwd_params_of(a, (int64_t)sh.c0 + sh.cfirst + threadIdx.x);
-            s.stab[2 * b + threadIdx.x] = make_float4(p.m, p.inv, p.g, p.b);
+            const int64_t c = (int64_t)sh.c0 + sh.cfirst + threadIdx.x;
+            // the forward's normalisation (batchnorm.zig:142), to recompute y from x
+            s.stab[2 * b + threadIdx.x] = make_float4(a.mean_in[c], 1.0f / (sqrtf(a.var_in[c]) + 0.000001f),
+                                                      a.scales[c], a.biases[c]);
         }
     }
 
@@ -1441,7 +766,10 @@ struct SweepKernel {
         if (lane == 0) {
             s.wrec[(2 * b + 0) * kSWarps + warp] = rec[0];
             s.wrec[(2 * b + 1) * kSWarps + warp] = rec[1];
+            __threadfence_block();
+            atomicAdd(&s.done[b], 1);
         }
+        __syncwarp();
     }
 
     // control warp: one record per segment from the streaming warps' partials of group g
@@ -1471,33 +799,6 @@ struct SweepKernel {
         // lane 0 wrote every record: its release-add publishes them
         if (lane == 0) asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(stats_done + g) : "memory");
         __syncwarp();
-    }
-
-    // control warp: bounded wait until every CTA counted itself in stats_done[g]
-    __device__ static bool wait_all(const PArgs &a, const unsigned *stats_done, int g) {
-        int ok = 1;
-        if ((threadIdx.x & 31) == 0) {
-            const unsigned *cnt = stats_done + g;
-            if (ld_acquire_gpu(cnt) < (unsigned)a.Ps) {
-                const unsigned long long deadline = global_ns() + a.wait_ns;
-                while (ld_acquire_gpu(cnt) < (unsigned)a.Ps) {
-                    if (ld_volatile(a.abort_flag)) {
-                        ok = 0;
-                        break;
-                    }
-                    if (global_ns() > deadline) {
-                        atomicOr(a.err, DEVERR_WAIT_BARRIER);
-                        atomicExch(a.abort_flag, 1u);
-                        ok = 0;
-                        break;
-                    }
-                    __nanosleep(64);
-                }
-            }
-        }
-        ok = __shfl_sync(0xffffffffu, ok, 0);
-        __syncwarp();  // lane 0's acquire orders the other lanes' record loads too
-        return ok != 0;
     }
 
     // control warp: merge the records of the (at most two) channels of CTA rid's share of
@@ -1678,59 +979,90 @@ __global__ void __launch_bounds__(kSThreads, kSMinBlocks) k_bn_sweep(PArgs a) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     const typename K::Smem s = K::carve(a, smem_raw);
     __shared__ unsigned s_epoch;
+    const int rid = (int)blockIdx.x;
     if (threadIdx.x == 0) {
         s_epoch = ld_volatile(&a.sync[0]);
         *s.stop = 0;
     }
+    if (threadIdx.x < a.G) {
+        s.done[threadIdx.x] = 0;
+        s.ready[threadIdx.x] = 0;
+    }
+    for (int g = 0; g < a.G; ++g) K::tabulate(a, s, g, rid, g);
     __syncthreads();
     const unsigned epoch = s_epoch;
     unsigned *stats_done = a.sync + 1 + (size_t)(epoch & 1u) * 2 * kMaxGroups;
-    const int rid = (int)blockIdx.x;
     const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
     if (warp == kSWarps) {
         // control warp
         if (rid == 0) {  // the next launch's bank
             unsigned *other = a.sync + 1 + (size_t)((epoch & 1u) ^ 1u) * 2 * kMaxGroups;
-            for (int i = threadIdx.x & 31; i < 2 * kMaxGroups; i += 32) other[i] = 0u;
+            for (int i = lane; i < 2 * kMaxGroups; i += 32) other[i] = 0u;
         }
-        for (int g = 0; g < a.G; ++g) {
-            const int b = g & 1;
-            bar_sync(kBarStats + b, kSThreads);  // the streaming warps' partials of group g
-            K::publish(a, s, g, rid, b, stats_done);
-            const bool ok = K::wait_all(a, stats_done, g);
-            // every CTA has read the epoch once all have counted themselves in group 0
-            if (ok && g == 0 && rid == 0 && (threadIdx.x & 31) == 0) atomicExch(&a.sync[0], epoch + 1);
-            if (ok) K::merge(a, s, g, rid, b);
-            else if ((threadIdx.x & 31) == 0) *s.stop = 1;
-            bar_arrive(kBarParams + b, kSThreads);
-            if (!ok) return;
+        int pub = 0, mrg = 0;  // next group to publish, next group to merge
+        unsigned long long deadline = global_ns() + a.wait_ns;
+        bool ok = true;
+        while (mrg < a.G) {
+            int what = 0;  // 1: publish group pub, 2: merge group mrg
+            if (lane == 0) {
+                if (pub < a.G && *reinterpret_cast<volatile int *>(&s.done[pub]) >= kSWarps) what = 1;
+                else if (mrg < pub && ld_acquire_gpu(stats_done + mrg) >= (unsigned)a.Ps) what = 2;
+                else if (ld_volatile(a.abort_flag)) what = 3;
+                else if (global_ns() > deadline) {
+                    atomicOr(a.err, DEVERR_WAIT_BARRIER);
+                    atomicExch(a.abort_flag, 1u);
+                    what = 3;
+                }
+            }
+            what = __shfl_sync(0xffffffffu, what, 0);
+            __syncwarp();  // lane 0's checks order the other lanes' reads
+            if (what == 3) {
+                ok = false;
+                break;
+            }
+            if (what == 0) {
+                __nanosleep(32);
+                continue;
+            }
+            if (what == 1) {
+                __threadfence_block();
+                K::publish(a, s, pub, rid, pub, stats_done);
+                ++pub;
+            } else {
+                // every CTA has read the epoch once all have counted themselves in group 0
+                if (mrg == 0 && rid == 0 && lane == 0) atomicExch(&a.sync[0], epoch + 1);
+                K::merge(a, s, mrg, rid, mrg);
+                if (lane == 0) {
+                    __threadfence_block();
+                    *reinterpret_cast<volatile int *>(&s.ready[mrg]) = 1;
+                }
+                __syncwarp();
+                ++mrg;
+            }
+            deadline = global_ns() + a.wait_ns;
         }
+        if (!ok && lane == 0) *reinterpret_cast<volatile int *>(s.stop) = 1;
         return;
     }
-    // streaming warps
-    K::tabulate(a, s, 0, rid, 0);
-    bar_sync(kBarStream, kStreamThreads);
-    K::stats(a, s, 0, rid, 0);
-    bar_arrive(kBarStats + 0, kSThreads);
+    // streaming warps: statistics of groups 0 .. lag-1, then per group g the statistics of
+    // group g + lag followed by the outputs of group g
+    for (int h = 0; h < a.depth && h < a.G; ++h) K::stats(a, s, h, rid, h);
     for (int g = 0; g < a.G; ++g) {
-        const int b = g & 1;
-        if (g + 1 < a.G) {
-            K::tabulate(a, s, g + 1, rid, b ^ 1);
-            bar_sync(kBarStream, kStreamThreads);
-            K::stats(a, s, g + 1, rid, b ^ 1);
-            bar_arrive(kBarStats + (b ^ 1), kSThreads);
-        }
-        bar_sync(kBarParams + b, kSThreads);  // group g's parameters are in s.ptab[b]
-        if (*s.stop) return;
-        K::apply(a, s, g, rid, b);
-        bar_sync(kBarStream, kStreamThreads);  // table b and s.ptab[b] are rewritten for group g+2
+        if (g + a.depth < a.G) K::stats(a, s, g + a.depth, rid, g + a.depth);
+        if (!K::wait_smem(a, s, &s.ready[g], 1)) return;  // group g's parameters
+        K::apply(a, s, g, rid, g);
     }
 }
 
-// Sweep plan: P = 2 CTAs per SM; units of U = spatial/K floats with K the smallest divisor
-// giving >= 8 units per CTA in a group (U >= 256 floats); groups of cg channels whose
-// inputs fill about DNB_BN_GROUP_MB (default 32 MiB) so that the group being written and
-// the group being reduced both stay in L2; cg <= P keeps a share within two channels.
+// Sweep plan: P = CTAs per SM x SMs; channel groups whose inputs fill about
+// DNB_BN_GROUP_MB (default 32 MiB), at most kMaxSweepGroups of them; lag = groups whose
+// statistics run ahead of the outputs, as many as keep lag + 1 groups within DNB_BN_L2_MB
+// (default 64 MiB) of L2, so that the grid exchange of a group is hidden behind later
+// statistics passes (or, when the whole input fits, every statistics pass runs before the
+// first output pass); units of U = spatial/K floats with K the smallest divisor giving
+// >= 8 units per CTA in a group (U >= 256 floats); cg <= P keeps a share within two
+// channels.
 template <bool BWD, bool HASY>
 PPlan plan_sweep(int64_t batch, int64_t filters, int64_t spatial, const DeviceState *ds, int occupancy) {
     using K = SweepKernel<BWD, DNB_ACT_LEAKY, HASY>;
@@ -1741,7 +1073,7 @@ PPlan plan_sweep(int64_t batch, int64_t filters, int64_t spatial, const DeviceSt
     if (ctas > 2048 / kSThreads) ctas = 2048 / kSThreads;
     const int64_t P = (int64_t)ds->sm_count * ctas;
     const int64_t bytes_per_channel = batch * spatial * 4 * nt;
-    const int64_t budget = (int64_t)env_int("DNB_BN_GROUP_MB", 32, 1, 4096) << 20;
+    const int64_t budget = ((int64_t)env_int("DNB_BN_GROUP_MB", 32, 1, 4096) << 20) * nt;
     int64_t cg = budget / bytes_per_channel;
     if (cg < 1) cg = 1;
     if (cg > P) cg = P;
@@ -1749,7 +1081,7 @@ PPlan plan_sweep(int64_t batch, int64_t filters, int64_t spatial, const DeviceSt
     int64_t G = (filters + cg - 1) / cg;
     cg = (filters + G - 1) / G;
     G = (filters + cg - 1) / cg;
-    if (G > kMaxGroups) return pl;
+    if (G > kMaxSweepGroups) return pl;
     int64_t k = 0;
     for (int64_t kk = 1; kk <= spatial; ++kk) {
         if (spatial % kk || (spatial / kk) % 4) continue;
@@ -1768,10 +1100,14 @@ PPlan plan_sweep(int64_t batch, int64_t filters, int64_t spatial, const DeviceSt
     pl.cg = (int)cg;
     pl.G = (int)G;
     pl.P = (int)P;
-    pl.depth = 2;
+    const int64_t l2 = ((int64_t)env_int("DNB_BN_L2_MB", 64, 1, 4096) << 20) * nt;
+    int64_t lag = l2 / (cg * bytes_per_channel) - 1;
+    if (lag > G - 1) lag = G - 1;
+    if (lag < 0) lag = 0;
+    pl.depth = (int)lag;
     pl.cap_units = (int)share;
     pl.ctas_per_sm = ctas;
-    pl.smem = K::smem_bytes(pl.cap_units);
+    pl.smem = K::smem_bytes(pl.cap_units, pl.G);
     size_t per_cta = (size_t)ds->smem_per_sm / ctas - (size_t)ds->smem_reserved - 256;
     if (per_cta > (size_t)ds->max_smem_optin) per_cta = (size_t)ds->max_smem_optin;
     pl.ok = pl.smem <= per_cta;
@@ -1779,8 +1115,7 @@ PPlan plan_sweep(int64_t batch, int64_t filters, int64_t spatial, const DeviceSt
 }
 
 // Fills the partition fields of `a` from a plan whose two roles have ps and pa CTAs.
-void fill_partition(PArgs &a, const PPlan &pl, int64_t batch, int64_t filters, int64_t spatial, int ps, int pa,
-                    int threads) {
+void fill_partition(PArgs &a, const PPlan &pl, int64_t batch, int64_t filters, int64_t spatial) {
     a.C = filters;
     a.S = spatial;
     a.N = (int)batch;
@@ -1789,19 +1124,14 @@ void fill_partition(PArgs &a, const PPlan &pl, int64_t batch, int64_t filters, i
     a.NK = (int)(batch * pl.K);
     a.cg = pl.cg;
     a.G = pl.G;
-    a.Ps = ps;
-    a.Pa = pa;
+    a.Ps = pl.P;
     a.depth = pl.depth;
     a.cap_units = pl.cap_units;
     a.T_full = (uint32_t)pl.cg * (uint32_t)a.NK;
     a.T_last = (uint32_t)(filters - (int64_t)(pl.G - 1) * pl.cg) * (uint32_t)a.NK;
-    a.f_u4 = FastDiv((uint32_t)(pl.U / 4));
-    a.step_q = (uint32_t)(threads / (pl.U / 4));
-    a.step_r = (uint32_t)(threads % (pl.U / 4));
     a.f_nk = FastDiv((uint32_t)a.NK);
     a.f_k = FastDiv((uint32_t)pl.K);
-    a.f_ps = FastDiv((uint32_t)ps);
-    a.f_pa = FastDiv((uint32_t)pa);
+    a.f_ps = FastDiv((uint32_t)pl.P);
     a.f_tfull = FastDiv(a.T_full);
     a.f_tlast = FastDiv(a.T_last);
     a.denom = (float)(spatial * batch);
@@ -1833,7 +1163,7 @@ dnb_status run_sweep(int64_t batch, int64_t filters, int64_t spatial, int act, P
         }
         Workspace *ws = nullptr;
         DNB_TRY(workspace(stream, sizeof(float4) * (size_t)pl.G * pl.P * 2, &ws));
-        fill_partition(a, pl, batch, filters, spatial, pl.P, pl.P, kSThreads);
+        fill_partition(a, pl, batch, filters, spatial);
         constexpr int chunk = SweepKernel<BWD, A, HASY>::CHUNK;
         a.cpu = (pl.U / 4 + chunk - 1) / chunk;
         a.f_cpu = FastDiv((uint32_t)a.cpu);
@@ -1859,23 +1189,10 @@ dnb_status run_sweep(int64_t batch, int64_t filters, int64_t spatial, int act, P
     });
 }
 
-bool use_pipeline_kernel() {
-    const char *e = getenv("DNB_BN_KERNEL");
-    return e && e[0] == 'p';
-}
-
 }  // namespace
 }  // namespace dnb
 
 using namespace dnb;
-
-#ifdef DNB_PHASE_TIMING
-extern "C" dnb_status dnb_debug_phase_times(unsigned long long *host, size_t count) {
-    DNB_CUDA(cudaDeviceSynchronize());
-    DNB_CUDA(cudaMemcpyFromSymbol(host, g_phase_ts, count * sizeof(unsigned long long)));
-    return DNB_OK;
-}
-#endif
 
 extern "C" {
 
@@ -1903,10 +1220,7 @@ dnb_status dnb_bn_act_forward_train(const float *x, float *y, float *x_norm, int
         a.rmean = rolling_mean;
         a.rvar = rolling_variance;
         bool launched = false;
-        if (use_pipeline_kernel())
-            DNB_TRY((run_persistent<false, false>(batch, filters, spatial, act, a, s, &launched, what)));
-        else
-            DNB_TRY((run_sweep<false, false>(batch, filters, spatial, act, a, s, &launched, what)));
+        DNB_TRY((run_sweep<false, false>(batch, filters, spatial, act, a, s, &launched, what)));
         if (launched) return DNB_OK;
     }
     const GGeom g = make_ggeom(batch, filters, spatial, aligned16(x));
@@ -1946,17 +1260,10 @@ dnb_status dnb_bn_act_backward(const float *x, const float *y, const float *delt
         a.mean_delta = mean_delta;
         a.var_delta = variance_delta;
         bool launched = false;
-        if (use_pipeline_kernel()) {
-            if (y)
-                DNB_TRY((run_persistent<true, true>(batch, filters, spatial, act, a, s, &launched, what)));
-            else
-                DNB_TRY((run_persistent<true, false>(batch, filters, spatial, act, a, s, &launched, what)));
-        } else {
-            if (y)
-                DNB_TRY((run_sweep<true, true>(batch, filters, spatial, act, a, s, &launched, what)));
-            else
-                DNB_TRY((run_sweep<true, false>(batch, filters, spatial, act, a, s, &launched, what)));
-        }
+        if (y)
+            DNB_TRY((run_sweep<true, true>(batch, filters, spatial, act, a, s, &launched, what)));
+        else
+            DNB_TRY((run_sweep<true, false>(batch, filters, spatial, act, a, s, &launched, what)));
         if (launched) return DNB_OK;
     }
     const GGeom g = make_ggeom(batch, filters, spatial, aligned16(x) && aligned16(delta) && (!y || aligned16(y)));

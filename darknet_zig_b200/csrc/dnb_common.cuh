@@ -53,25 +53,16 @@ struct DeviceState {
 // Scratch owned by the library for one (device, stream) pair.
 struct Workspace {
     cudaStream_t stream = nullptr;
-    // grid-barrier state: [0] = launch epoch, [1..] two banks of per-group arrival counters,
-    // then the sweep kernel's per-channel region (kChanStart ..)
+    // grid-barrier state: [0] = launch epoch, [1..] two banks of per-group arrival counters
     unsigned *sync = nullptr;
     size_t sync_words = 0;
     void *scratch = nullptr;  // per-channel partial records
     size_t scratch_bytes = 0;
 };
 
-// `sync` = 1 epoch word + 2 banks, each holding two arrays of kMaxGroups group counters,
-// then the per-channel region of the sweep kernel: a start counter, per-channel arrival
-// counters (each reset to 0 by its last arrival) and ready tags (the launch epoch once the
-// channel's parameters are published), and the published parameters (8 floats a channel).
+// `sync` = 1 epoch word + 2 banks, each holding two arrays of kMaxGroups group counters.
 constexpr int kMaxGroups = 1024;
-constexpr int kMaxChannels = 65536;
-constexpr size_t kChanStart = (1 + 4 * (size_t)kMaxGroups + 15) & ~(size_t)15;
-constexpr size_t kChanCount = kChanStart + 16;
-constexpr size_t kChanReady = kChanCount + kMaxChannels;
-constexpr size_t kChanParams = kChanReady + kMaxChannels;
-constexpr size_t kSyncWords = kChanParams + 8 * (size_t)kMaxChannels;
+constexpr size_t kSyncWords = 1 + 4 * (size_t)kMaxGroups;
 
 // The state of the current device, initialising it on first use.
 dnb_status current_device(DeviceState **out);
