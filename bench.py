@@ -66,6 +66,9 @@ def parse():
                          "together, with no flush kernel (each kernel also writes back the previous "
                          "one's dirty outputs, as in a training step); or read a 256 MiB buffer before "
                          "each kernel (L2 left clean); or write one (L2 left full of dirty lines)")
+    ap.add_argument("--syncbn", choices=["fused", "split"], default="fused",
+                    help="N > 1: statistics exchanged inside the fused kernels over NVLink (fused) or by "
+                         "NCCL collectives between split kernels (split)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     a = ap.parse_args()
@@ -229,7 +232,7 @@ def run_ours(a):
         elif a.flush == "write":
             flush_buf.fill_(1.0)
 
-    layer = syncbn.SyncBN(B, C, S, world=world, dist=dist)
+    layer = syncbn.SyncBN(B, C, S, world=world, dist=dist, fused=a.syncbn == "fused", rank=rank)
 
     def fwd(k):
         sx, sd, sy, sdx = sets[k % n_sets]
@@ -301,6 +304,8 @@ def run_ours(a):
     if not a.no_e2e:
         e2e = run_e2e(a, layer, x, y, delta, dx, gamma, beta, mean, var, rm, rv, bu, su, md, vd, dev, dist, world)
 
+    torch.cuda.synchronize()
+    layer.close()
     if dist:
         # release NCCL state before the process group goes away
         dist.barrier()
@@ -334,7 +339,7 @@ def run_ours(a):
                           f"256 MiB buffer {'read' if a.flush == 'read' else 'written'} before every timed "
                           f"kernel (cold L2{'' if a.flush == 'read' else ', full of dirty lines'})")
                          + f"; {E * 4 / 2**20:.0f} MiB tensors",
-                   "parallelism": f"dp{world}" + (" + sync-BN" if world > 1 else "")},
+                   "parallelism": f"dp{world}" + (f" + sync-BN ({a.syncbn})" if world > 1 else "")},
         "elems_per_s": round(E * world / (ms_step * 1e-3), 1),
         "pct_of_8TBs": round(100.0 * value / world / HBM_NOMINAL_GBS, 2),
         "kernels": {

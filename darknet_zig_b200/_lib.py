@@ -22,6 +22,7 @@ _CTYPES = {
     "float": C.c_float,
     "size_t": C.c_size_t,
     "dnb_stream": C.c_void_p,
+    "dnb_comm": C.c_void_p,
     "dnb_status": C.c_int,
 }
 

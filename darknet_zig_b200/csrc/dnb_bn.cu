@@ -451,6 +451,16 @@ struct PArgs {
     unsigned *sync;           // [0] epoch, then 2 banks of {stats_done[kMaxGroups], apply_done[kMaxGroups]}
     unsigned *err, *abort_flag;
     unsigned long long wait_ns;
+    // sync-BN across GPUs (xon, any world >= 1): rank r's exchange buffer holds, for each launch
+    // parity, channel and source rank, one double2 record and one ready tag; xrec/xflag[r]
+    // point into rank r's buffer (a peer mapping, or this GPU's own buffer for r == rank)
+    int xon, world, rank;
+    unsigned xtag;            // this launch's tag (the communicator's call number)
+    int xpar;                 // xtag & 1: which half of the buffers this launch uses
+    int64_t xcmax;            // channels the buffers hold
+    double xcount;            // elements of one channel on one rank (batch*spatial)
+    double2 *xrec[kMaxRanks];
+    unsigned *xflag[kMaxRanks];
 };
 
 // Share of CTA p of a role with `parts` CTAs in group g: units [t0, t1) of the group's T,
@@ -595,14 +605,16 @@ struct SweepKernel {
         float4 *wrec;    // [G][2 segments][kSWarps] per-warp partials
         float *ptab;     // [G][2 segments][8] apply parameters
         float4 *stab;    // [G][2 segments] forward parameters for the backward's stats
+        double2 *lrec;   // [G][2 segments] this rank's merged records: (mean, M2) or (sum g, sum g(x-m))
+        double *lcnt;    // [G][2 segments] elements behind the forward's records
         int *done;       // [G] streaming warps that have left their partials of group g
         int *ready;      // [G] 1 once the parameters of group g are in ptab
         int *stop;       // set by the control warp when a wait gave up
     };
     __host__ __device__ static size_t smem_bytes(int cap_units, int groups) {
         return (((size_t)groups * cap_units * sizeof(uint32_t) + 15) & ~(size_t)15) +
-               (size_t)groups * (2 * kSWarps * sizeof(float4) + 16 * sizeof(float) + 2 * sizeof(float4) +
-                                 2 * sizeof(int)) +
+               (size_t)groups * (2 * kSWarps * sizeof(float4) + 2 * sizeof(double2) + 2 * sizeof(double) +
+                                 16 * sizeof(float) + 2 * sizeof(float4) + 2 * sizeof(int)) +
                16;
     }
     __device__ static Smem carve(const PArgs &a, unsigned char *raw) {
@@ -613,6 +625,10 @@ struct SweepKernel {
         o += ((size_t)G * a.cap_units * sizeof(uint32_t) + 15) & ~(size_t)15;
         s.wrec = reinterpret_cast<float4 *>(raw + o);
         o += (size_t)G * 2 * kSWarps * sizeof(float4);
+        s.lrec = reinterpret_cast<double2 *>(raw + o);
+        o += (size_t)G * 2 * sizeof(double2);
+        s.lcnt = reinterpret_cast<double *>(raw + o);
+        o += (size_t)G * 2 * sizeof(double);
         s.stab = reinterpret_cast<float4 *>(raw + o);
         o += (size_t)G * 2 * sizeof(float4);
         s.ptab = reinterpret_cast<float *>(raw + o);
@@ -801,30 +817,18 @@ struct SweepKernel {
         __syncwarp();
     }
 
-    // control warp: merge the records of the (at most two) channels of CTA rid's share of
-    // group g into the apply parameters s.ptab[b]; the CTA owning a channel's first unit
-    // writes the per-channel outputs. Records of CTAs between the channel's first and last
-    // owner that hold no unit of it (a group with fewer units than CTAs) are skipped.
-    __device__ static void merge(const PArgs &a, const Smem &s, int g, int rid, int b) {
+    // control warp: merge this rank's records of the (at most two) channels of CTA rid's
+    // share of group g into s.lrec[g]; with a communicator, the CTA owning a channel's first
+    // unit then stores the merged record into every rank's exchange buffer over NVLink and
+    // tags it. Records of CTAs between the channel's first and last owner that hold no unit
+    // of it (a group with fewer units than CTAs) are skipped.
+    __device__ static void merge_local(const PArgs &a, const Smem &s, int g, int rid) {
         const Share sh = share_of(a, g, rid, a.f_ps);
         const int lane = threadIdx.x & 31;
         for (int j = 0; j < sh.nseg; ++j) {
             const int cl = sh.cfirst + j;
             const int64_t c = (int64_t)sh.c0 + cl;
-            float gamma = 0.0f, beta = 0.0f, m_in = 0.0f, v_in = 0.0f, rm = 0.0f, rv = 0.0f;
             const uint32_t ua = (uint32_t)cl * a.NK, ub = ua + a.NK;
-            const bool write = owner_of(a, g, ua, a.Ps) == rid;
-            if (lane == 0) {
-                gamma = a.scales[c];
-                beta = a.biases[c];
-                if constexpr (BWD) {
-                    m_in = a.mean_in[c];
-                    v_in = a.var_in[c];
-                } else if (write) {
-                    rm = a.rmean[c];
-                    rv = a.rvar[c];
-                }
-            }
             const int plo = owner_of(a, g, ua, a.Ps), phi = owner_of(a, g, ub - 1, a.Ps);
             const int nrec = phi - plo + 1;
             auto load = [&](int idx, float4 &dst) -> bool {
@@ -843,7 +847,7 @@ struct SweepKernel {
                 const int idx = lane + 32 * k;
                 have[k] = idx < nrec && load(idx, r[k]);
             }
-            float *out = s.ptab + (2 * b + j) * 8;
+            double2 mine;
             if constexpr (!BWD) {
                 double sn = 0.0, smn = 0.0;
 #pragma unroll
@@ -874,16 +878,8 @@ struct SweepKernel {
                     m2 += (double)t.z + (double)t.x * d * d;
                 }
                 m2 = warp_sum(m2);
-                if (lane == 0) {
-                    const FwdClose f = fwd_close(mu, m2, sn);
-                    if (write) {
-                        a.mean[c] = f.m;
-                        a.var[c] = f.var;
-                        a.rmean[c] = rolling(rm, f.m);
-                        a.rvar[c] = rolling(rv, f.var);
-                    }
-                    *reinterpret_cast<float4 *>(out) = make_float4(f.m, f.inv, gamma, beta);
-                }
+                mine = make_double2(mu, m2);
+                if (lane == 0) s.lcnt[2 * g + j] = sn;
             } else {
                 double s1 = 0.0, s2 = 0.0;
 #pragma unroll
@@ -898,11 +894,91 @@ struct SweepKernel {
                     s1 += (double)t.x;
                     s2 += (double)t.y;
                 }
-                s1 = warp_sum(s1);
-                s2 = warp_sum(s2);
-                if (lane == 0) {
-                    const BwdParam bp = bwd_close(s1, s2, m_in, v_in, gamma, beta, a.denom, a.bias_upd, a.scale_upd,
-                                                  a.mean_delta, a.var_delta, c, write);
+                mine = make_double2(warp_sum(s1), warp_sum(s2));
+            }
+            if (lane == 0) s.lrec[2 * g + j] = mine;
+            if (a.xon && plo == rid && lane < a.world) {
+                // this CTA owns the channel's first unit: send the record to rank `lane`
+                const size_t slot = ((size_t)a.xpar * a.xcmax + c) * a.world + a.rank;
+                asm volatile("st.global.v2.f64 [%0], {%1, %2};" ::"l"(a.xrec[lane] + slot), "d"(mine.x),
+                             "d"(mine.y)
+                             : "memory");
+                asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a.xflag[lane] + slot), "r"(a.xtag)
+                             : "memory");
+            }
+        }
+        __syncwarp();
+    }
+
+    // control warp, with a communicator: have every rank's records of the channels of CTA
+    // rid's share of group g arrived in this GPU's buffer? (warp-uniform; acquires them)
+    __device__ static bool peers_ready(const PArgs &a, int g, int rid) {
+        const Share sh = share_of(a, g, rid, a.f_ps);
+        const int lane = threadIdx.x & 31;
+        bool ok = true;
+        for (int j = 0; j < sh.nseg; ++j) {
+            if (lane < a.world) {
+                const int64_t c = (int64_t)sh.c0 + sh.cfirst + j;
+                const unsigned *flag = a.xflag[a.rank] + ((size_t)a.xpar * a.xcmax + c) * a.world + lane;
+                unsigned v;
+                asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+                ok = ok && v == a.xtag;
+            }
+        }
+        return __all_sync(0xffffffffu, ok) != 0;
+    }
+
+    // control warp: the statistics of the channels of CTA rid's share of group g -- this
+    // rank's merged records, combined in rank order with the other ranks' (same order,
+    // same result on every rank) -- closed into the apply parameters s.ptab[g]; the CTA
+    // owning a channel's first unit writes the per-channel outputs.
+    __device__ static void finalize(const PArgs &a, const Smem &s, int g, int rid) {
+        const Share sh = share_of(a, g, rid, a.f_ps);
+        const int lane = threadIdx.x & 31;
+        for (int j = 0; j < sh.nseg; ++j) {
+            const int cl = sh.cfirst + j;
+            const int64_t c = (int64_t)sh.c0 + cl;
+            const uint32_t ua = (uint32_t)cl * a.NK;
+            const bool write = owner_of(a, g, ua, a.Ps) == rid;
+            double2 tot = s.lrec[2 * g + j];
+            double n = s.lcnt[2 * g + j];
+            if (a.xon) {
+                double2 r2 = make_double2(0.0, 0.0);
+                const bool in = lane < a.world;
+                if (in) {
+                    const double2 *src = a.xrec[a.rank] + ((size_t)a.xpar * a.xcmax + c) * a.world + lane;
+                    asm volatile("ld.relaxed.sys.global.v2.f64 {%0, %1}, [%2];"
+                                 : "=d"(r2.x), "=d"(r2.y)
+                                 : "l"(src)
+                                 : "memory");
+                }
+                if constexpr (!BWD) {
+                    // every rank holds a.xcount elements of the channel: Chan's merge of the
+                    // ranks' (mean, M2), lanes in rank order
+                    n = a.xcount * a.world;
+                    const double mu = warp_sum(in ? r2.x : 0.0) / a.world;
+                    const double d = in ? r2.x - mu : 0.0;
+                    tot = make_double2(mu, warp_sum(in ? r2.y + a.xcount * d * d : 0.0));
+                } else {
+                    tot = make_double2(warp_sum(in ? r2.x : 0.0), warp_sum(in ? r2.y : 0.0));
+                }
+            }
+            if (lane == 0) {
+                float *out = s.ptab + (2 * g + j) * 8;
+                const float gamma = a.scales[c], beta = a.biases[c];
+                if constexpr (!BWD) {
+                    const FwdClose f = fwd_close(tot.x, tot.y, n);
+                    if (write) {
+                        const float rm = a.rmean[c], rv = a.rvar[c];
+                        a.mean[c] = f.m;
+                        a.var[c] = f.var;
+                        a.rmean[c] = rolling(rm, f.m);
+                        a.rvar[c] = rolling(rv, f.var);
+                    }
+                    *reinterpret_cast<float4 *>(out) = make_float4(f.m, f.inv, gamma, beta);
+                } else {
+                    const BwdParam bp = bwd_close(tot.x, tot.y, a.mean_in[c], a.var_in[c], gamma, beta, a.denom,
+                                                  a.bias_upd, a.scale_upd, a.mean_delta, a.var_delta, c, write);
                     *reinterpret_cast<BwdParam *>(out) = bp;
                 }
             }
@@ -1000,24 +1076,31 @@ __global__ void __launch_bounds__(kSThreads, kSMinBlocks) k_bn_sweep(PArgs a) {
             unsigned *other = a.sync + 1 + (size_t)((epoch & 1u) ^ 1u) * 2 * kMaxGroups;
             for (int i = lane; i < 2 * kMaxGroups; i += 32) other[i] = 0u;
         }
-        int pub = 0, mrg = 0;  // next group to publish, next group to merge
+        // groups move through: published (pub) -> merged on this rank and, with a
+        // communicator, sent to the other ranks (loc) -> finalised, parameters in shared
+        // memory (fin); no step waits behind another group's
+        int pub = 0, loc = 0, fin = 0;
         unsigned long long deadline = global_ns() + a.wait_ns;
         bool ok = true;
-        while (mrg < a.G) {
-            int what = 0;  // 1: publish group pub, 2: merge group mrg
+        while (fin < a.G) {
+            int what = 0;  // 1: publish group pub, 2: finalise group fin, 3: merge group loc
             if (lane == 0) {
                 if (pub < a.G && *reinterpret_cast<volatile int *>(&s.done[pub]) >= kSWarps) what = 1;
-                else if (mrg < pub && ld_acquire_gpu(stats_done + mrg) >= (unsigned)a.Ps) what = 2;
-                else if (ld_volatile(a.abort_flag)) what = 3;
+                else if (loc < pub && ld_acquire_gpu(stats_done + loc) >= (unsigned)a.Ps) what = 3;
+            }
+            what = __shfl_sync(0xffffffffu, what, 0);
+            if (what == 0 && a.xon && fin < loc && K::peers_ready(a, fin, rid)) what = 2;
+            if (what == 0 && lane == 0) {
+                if (ld_volatile(a.abort_flag)) what = 4;
                 else if (global_ns() > deadline) {
-                    atomicOr(a.err, DEVERR_WAIT_BARRIER);
+                    atomicOr(a.err, fin < loc ? DEVERR_WAIT_PEER : DEVERR_WAIT_BARRIER);
                     atomicExch(a.abort_flag, 1u);
-                    what = 3;
+                    what = 4;
                 }
             }
             what = __shfl_sync(0xffffffffu, what, 0);
             __syncwarp();  // lane 0's checks order the other lanes' reads
-            if (what == 3) {
+            if (what == 4) {
                 ok = false;
                 break;
             }
@@ -1029,16 +1112,21 @@ __global__ void __launch_bounds__(kSThreads, kSMinBlocks) k_bn_sweep(PArgs a) {
                 __threadfence_block();
                 K::publish(a, s, pub, rid, pub, stats_done);
                 ++pub;
-            } else {
+            } else if (what == 3) {
                 // every CTA has read the epoch once all have counted themselves in group 0
-                if (mrg == 0 && rid == 0 && lane == 0) atomicExch(&a.sync[0], epoch + 1);
-                K::merge(a, s, mrg, rid, mrg);
+                if (loc == 0 && rid == 0 && lane == 0) atomicExch(&a.sync[0], epoch + 1);
+                K::merge_local(a, s, loc, rid);
+                ++loc;
+                if (!a.xon) what = 2;  // nothing to wait for
+            }
+            if (what == 2) {
+                K::finalize(a, s, fin, rid);
                 if (lane == 0) {
                     __threadfence_block();
-                    *reinterpret_cast<volatile int *>(&s.ready[mrg]) = 1;
+                    *reinterpret_cast<volatile int *>(&s.ready[fin]) = 1;
                 }
                 __syncwarp();
-                ++mrg;
+                ++fin;
             }
             deadline = global_ns() + a.wait_ns;
         }
@@ -1143,7 +1231,7 @@ void fill_partition(PArgs &a, const PPlan &pl, int64_t batch, int64_t filters, i
 
 template <bool BWD, bool HASY>
 dnb_status run_sweep(int64_t batch, int64_t filters, int64_t spatial, int act, PArgs a, cudaStream_t stream,
-                     bool *launched, const char *what) {
+                     bool *launched, const char *what, const CommView *cv = nullptr) {
     *launched = false;
     DeviceState *ds = nullptr;
     DNB_TRY(current_device(&ds));
@@ -1173,6 +1261,26 @@ dnb_status run_sweep(int64_t batch, int64_t filters, int64_t spatial, int act, P
         a.err = ds->error_word;
         a.abort_flag = ds->abort_flag;
         a.wait_ns = wait_limit_ns();
+        a.xon = 0;
+        a.world = 1;
+        if (cv) {
+            a.xon = 1;
+            a.world = cv->world;
+            a.rank = cv->rank;
+            a.xtag = cv->tag;
+            a.xpar = (int)(cv->tag & 1u);
+            a.xcmax = cv->cmax;
+            a.xcount = (double)(batch * spatial);
+            for (int r = 0; r < cv->world; ++r) {
+                a.xrec[r] = static_cast<double2 *>(cv->rec[r]);
+                a.xflag[r] = cv->flag[r];
+            }
+            // normalize_delta divides by the element count of the whole batch
+            a.denom = (float)(batch * spatial * cv->world);
+            int e2 = 0;
+            a.denom_pow2 = frexpf(a.denom, &e2) == 0.5f;
+            a.inv_denom = 1.0f / a.denom;
+        }
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3((unsigned)pl.P);
         cfg.blockDim = dim3(kSThreads);
@@ -1273,6 +1381,79 @@ dnb_status dnb_bn_act_backward(const float *x, const float *y, const float *delt
     DNB_TRY(generic_bwd_partials(g, x, y, delta, mean, variance, scales, biases, act, sc, s));
     return generic_bwd_apply(g, x, y, delta, dx, (float)(spatial * batch), sc.local, scales, biases, mean, variance,
                              bias_updates, scale_updates, mean_delta, variance_delta, act, sc, s);
+}
+
+dnb_status dnb_syncbn_act_forward_train(dnb_comm comm, const float *x, float *y, float *x_norm, int64_t batch,
+                                        int64_t filters, int64_t spatial, const float *scales, const float *biases,
+                                        float *mean, float *variance, float *rolling_mean,
+                                        float *rolling_variance, int act, dnb_stream stream) {
+    const char *what = "syncbn_act_forward_train";
+    DNB_TRY(check_shape(batch, filters, spatial, what));
+    if (!valid_act(act)) return fail(DNB_ERR_INVALID, "%s: unknown activation %d", what, act);
+    if (filters == 0) return DNB_OK;
+    if (!x || !y || !scales || !biases || !mean || !variance || !rolling_mean || !rolling_variance)
+        return fail(DNB_ERR_INVALID, "%s: null pointer", what);
+    CommView cv;
+    DNB_TRY(comm_next(comm, &cv));
+    if (filters > cv.cmax) return fail(DNB_ERR_UNSUPPORTED, "%s: %lld channels, communicator holds %lld", what,
+                                       (long long)filters, (long long)cv.cmax);
+    if (!(aligned16(x) && aligned16(y) && (!x_norm || aligned16(x_norm))))
+        return fail(DNB_ERR_UNSUPPORTED, "%s: tensors must be 16-byte aligned", what);
+    PArgs a{};
+    a.t0 = x;
+    a.out = y;
+    a.xnorm = x_norm;
+    a.scales = scales;
+    a.biases = biases;
+    a.mean = mean;
+    a.var = variance;
+    a.rmean = rolling_mean;
+    a.rvar = rolling_variance;
+    bool launched = false;
+    DNB_TRY((run_sweep<false, false>(batch, filters, spatial, act, a, as_stream(stream), &launched, what, &cv)));
+    if (!launched) return fail(DNB_ERR_UNSUPPORTED, "%s: shape not taken by the fused kernel", what);
+    return DNB_OK;
+}
+
+dnb_status dnb_syncbn_act_backward(dnb_comm comm, const float *x, const float *y, const float *delta, float *dx,
+                                   int64_t batch, int64_t filters, int64_t spatial, const float *scales,
+                                   const float *biases, const float *mean, const float *variance,
+                                   float *bias_updates, float *scale_updates, float *mean_delta,
+                                   float *variance_delta, int act, dnb_stream stream) {
+    const char *what = "syncbn_act_backward";
+    DNB_TRY(check_shape(batch, filters, spatial, what));
+    if (!valid_act(act)) return fail(DNB_ERR_INVALID, "%s: unknown activation %d", what, act);
+    if (filters == 0) return DNB_OK;
+    if (!x || !delta || !dx || !scales || !biases || !mean || !variance || !bias_updates || !scale_updates ||
+        !mean_delta || !variance_delta)
+        return fail(DNB_ERR_INVALID, "%s: null pointer", what);
+    CommView cv;
+    DNB_TRY(comm_next(comm, &cv));
+    if (filters > cv.cmax) return fail(DNB_ERR_UNSUPPORTED, "%s: %lld channels, communicator holds %lld", what,
+                                       (long long)filters, (long long)cv.cmax);
+    if (!(aligned16(x) && aligned16(delta) && aligned16(dx) && (!y || aligned16(y))))
+        return fail(DNB_ERR_UNSUPPORTED, "%s: tensors must be 16-byte aligned", what);
+    PArgs a{};
+    a.t0 = delta;
+    a.t1 = x;
+    a.t2 = y;
+    a.out = dx;
+    a.scales = scales;
+    a.biases = biases;
+    a.mean_in = mean;
+    a.var_in = variance;
+    a.bias_upd = bias_updates;
+    a.scale_upd = scale_updates;
+    a.mean_delta = mean_delta;
+    a.var_delta = variance_delta;
+    bool launched = false;
+    const cudaStream_t s = as_stream(stream);
+    if (y)
+        DNB_TRY((run_sweep<true, true>(batch, filters, spatial, act, a, s, &launched, what, &cv)));
+    else
+        DNB_TRY((run_sweep<true, false>(batch, filters, spatial, act, a, s, &launched, what, &cv)));
+    if (!launched) return fail(DNB_ERR_UNSUPPORTED, "%s: shape not taken by the fused kernel", what);
+    return DNB_OK;
 }
 
 dnb_status dnb_syncbn_forward_partials(const float *x, int64_t batch, int64_t filters, int64_t spatial,

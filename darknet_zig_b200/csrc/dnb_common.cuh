@@ -64,6 +64,19 @@ struct Workspace {
 constexpr int kMaxGroups = 1024;
 constexpr size_t kSyncWords = 1 + 4 * (size_t)kMaxGroups;
 
+// A sync-BN communicator as a kernel sees it (dnb_comm.cu): this rank, the ranks, the call
+// number of the launch and every rank's exchange buffer (records, then ready tags).
+constexpr int kMaxRanks = 8;
+struct CommView {
+    int rank = 0, world = 1;
+    unsigned tag = 0;
+    int64_t cmax = 0;
+    void *rec[kMaxRanks] = {};
+    unsigned *flag[kMaxRanks] = {};
+};
+// The view of `comm` for its next fused call on the current device (advances its call number).
+dnb_status comm_next(dnb_comm comm, CommView *out);
+
 // The state of the current device, initialising it on first use.
 dnb_status current_device(DeviceState **out);
 // The workspace of (current device, stream) with at least `scratch_bytes` of scratch.

@@ -238,3 +238,47 @@ def sgdMomentum(n, weights, weight_updates, learning_rate, momentum, decay, batc
 def softmaxXent(input, truth, n, batch, temp, output, delta, err, cost=None):  # noqa: N802,A002
     call("softmax_xent", _p(input), _p(truth), int(n), int(batch), float(temp), _p(output), _p(delta), _p(err),
          _p(cost), _s())
+
+
+# ---- fused sync-BN across GPUs (no reference counterpart) --------------------------------
+
+def commInit(rank: int, world: int, max_channels: int):  # noqa: N802
+    """A sync-BN communicator on the current device: (handle, this rank's 64-byte IPC handle)."""
+    import ctypes
+
+    comm = ctypes.c_void_p(0)
+    ipc = ctypes.create_string_buffer(64)
+    call("comm_init", int(rank), int(world), int(max_channels), ipc, ctypes.byref(comm))
+    return comm.value, ipc.raw
+
+
+def commConnect(comm, handles: bytes) -> None:  # noqa: N802
+    """Opens the peers' exchange buffers; handles = every rank's 64-byte IPC handle, rank order."""
+    import ctypes
+
+    call("comm_connect", ctypes.c_void_p(comm), ctypes.create_string_buffer(bytes(handles), len(handles)))
+
+
+def commDestroy(comm) -> None:  # noqa: N802
+    import ctypes
+
+    call("comm_destroy", ctypes.c_void_p(comm))
+
+
+def syncbnActForwardTrain(comm, x, y, x_norm, batch, filters, spatial, scales, biases, mean_out,  # noqa: N802
+                          variance_out, rolling_mean, rolling_variance, act):
+    import ctypes
+
+    call("syncbn_act_forward_train", ctypes.c_void_p(comm), _p(x), _p(y), _p(x_norm), int(batch), int(filters),
+         int(spatial), _p(scales), _p(biases), _p(mean_out), _p(variance_out), _p(rolling_mean),
+         _p(rolling_variance), int(act), _s())
+
+
+def syncbnActBackward(comm, x, y, delta, dx, batch, filters, spatial, scales, biases, mean_in,  # noqa: N802
+                      variance_in, bias_updates, scale_updates, mean_delta_out, variance_delta_out, act):
+    import ctypes
+
+    call("syncbn_act_backward", ctypes.c_void_p(comm), _p(x), _p(y), _p(delta), _p(dx), int(batch), int(filters),
+         int(spatial), _p(scales), _p(biases), _p(mean_in), _p(variance_in), _p(bias_updates), _p(scale_updates),
+         _p(mean_delta_out), _p(variance_delta_out), int(act), _s())
+

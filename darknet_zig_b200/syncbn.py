@@ -5,13 +5,18 @@ its batchnorm layer (batchnorm.zig:129-174) for BASELINE config 4. One process p
 each rank holds batch/world images.
 
   world == 1: the fused single-GPU kernels (dnb_bn_act_forward_train / _backward).
-  world  > 1: the split entry points around two small collectives per layer step:
+  world  > 1, fused (default): dnb_syncbn_act_forward_train / _backward on a communicator
+              (dnb_comm_*): one kernel per direction that exchanges the per-channel records
+              with the other GPUs itself, over NVLink peer memory, while it streams; the host
+              only swaps the communicator's IPC handles once (here through the process group).
+  world  > 1, split (shapes the fused kernel does not take, or fused=False): the split
+              entry points around two small collectives per layer step:
     forward   dnb_syncbn_forward_partials -> all_gather of [C,2] fp64 (mean, M2) per rank
               -> dnb_syncbn_forward_apply (Chan merge of the ranks' records, then apply)
     backward  dnb_syncbn_backward_partials -> all_reduce(SUM) of [C,2] fp64 (sum g,
               sum g*(x-mean)) -> dnb_syncbn_backward_apply
-The collectives go through a torch.distributed process group (NCCL on GPUs; the same
-exchange functions run over gloo on the CPU in tests/test_syncbn_cpu.py).
+The split path's collectives go through a torch.distributed process group (NCCL on GPUs;
+the same exchange functions run over gloo on the CPU in tests/test_syncbn_cpu.py).
 
 `combine_forward_partials` is the host restatement of the merge the device performs
 (k_fwd_finalize), used to check the protocol without a GPU.
@@ -65,13 +70,26 @@ def reduce_backward_partials(dist, part) -> None:
 
 
 class SyncBN:
-    def __init__(self, batch: int, filters: int, spatial: int, world: int = 1, dist=None):
+    def __init__(self, batch: int, filters: int, spatial: int, world: int = 1, dist=None, fused: bool = True,
+                 rank: int = 0):
         self.batch, self.filters, self.spatial = batch, filters, spatial
         self.world = world
         self.dist = dist
         if world > 1 and dist is None:
             raise ValueError("world > 1 needs a torch.distributed module with an initialised process group")
         self._bufs = None
+        self.comm = None
+        if world > 1 and fused:
+            # every rank's IPC handle, swapped once through the process group
+            self.comm, handle = gpu.commInit(rank, world, filters)
+            handles = [None] * world
+            dist.all_gather_object(handles, handle)
+            gpu.commConnect(self.comm, b"".join(handles))
+
+    def close(self) -> None:
+        if self.comm is not None:
+            gpu.commDestroy(self.comm)
+            self.comm = None
 
     def _buffers(self, device):
         import torch
@@ -85,14 +103,14 @@ class SyncBN:
             }
         return self._bufs
 
-    def launches_per_step(self) -> int:
-        """Kernels of this library one forward + backward launches."""
-        return 2 if self.world == 1 else 8
-
     def forward(self, x, y, gamma, beta, mean, var, rolling_mean, rolling_variance, act, x_norm=None):
         B, C, S = self.batch, self.filters, self.spatial
         if self.world == 1:
             gpu.bnActForwardTrain(x, y, x_norm, B, C, S, gamma, beta, mean, var, rolling_mean, rolling_variance, act)
+            return
+        if self.comm is not None:
+            gpu.syncbnActForwardTrain(self.comm, x, y, x_norm, B, C, S, gamma, beta, mean, var, rolling_mean,
+                                      rolling_variance, act)
             return
         b = self._buffers(x.device)
         s = gpu._s()
@@ -108,6 +126,10 @@ class SyncBN:
         if self.world == 1:
             gpu.bnActBackward(x, y, delta, dx, B, C, S, gamma, beta, mean, var, bias_updates, scale_updates,
                               mean_delta, variance_delta, act)
+            return
+        if self.comm is not None:
+            gpu.syncbnActBackward(self.comm, x, y, delta, dx, B, C, S, gamma, beta, mean, var, bias_updates,
+                                  scale_updates, mean_delta, variance_delta, act)
             return
         b = self._buffers(x.device)
         s = gpu._s()

@@ -33,6 +33,7 @@ extern "C" {
 
 typedef int dnb_status;
 typedef void *dnb_stream; /* a cudaStream_t / CUstream; NULL = legacy default stream */
+typedef void *dnb_comm;   /* a sync-BN communicator (dnb_comm_init); NULL = none */
 
 enum {
     DNB_OK = 0,
@@ -259,6 +260,39 @@ dnb_status dnb_softmax_xent(const float *input, const float *truth, int64_t n, i
  * the GPU race, so serialise them. */
 dnb_status dnb_mean_noalloc(const float *x, int64_t batch, int64_t filters, int64_t spatial, float *out,
                             dnb_stream stream);
+
+/* ------------------------------------------------------------------------------------ */
+/* fused sync-BN across GPUs: no counterpart in the reference (it trains on one GPU); the  */
+/* data-parallel form of the fused batchnorm entries, the statistics exchanged inside the  */
+/* kernel over NVLink peer memory                                                          */
+/* ------------------------------------------------------------------------------------ */
+
+/* One process (or thread) per GPU, `world` ranks (<= 8). On the rank's device: allocates this
+ * rank's exchange buffer for up to `max_channels` channels and writes its CUDA IPC handle
+ * (64 bytes) to handle_out. The caller passes every rank's handle, in rank order, to
+ * dnb_comm_connect on every rank (any host transport). */
+dnb_status dnb_comm_init(int rank, int world, int64_t max_channels, void *handle_out, dnb_comm *comm);
+/* Opens the peers' buffers (handles: world x 64 bytes, rank order). */
+dnb_status dnb_comm_connect(dnb_comm comm, const void *handles);
+dnb_status dnb_comm_destroy(dnb_comm comm);
+/* dnb_bn_act_forward_train with the statistics of the whole data-parallel batch: every rank
+ * passes its shard (the same batch, filters and spatial on every rank) and gets identical
+ * mean, variance and rolling statistics. Every rank must make the same sequence of fused
+ * sync-BN calls on a communicator, from one host thread per rank. Needs spatial % 4 == 0,
+ * 16-byte aligned tensors and filters <= max_channels; DNB_ERR_UNSUPPORTED otherwise (the
+ * split entries below then apply). A rank that never makes its call leaves the others'
+ * kernels waiting until the wait limit; they return DNB_ERR_TIMEOUT. */
+dnb_status dnb_syncbn_act_forward_train(dnb_comm comm, const float *x, float *y, float *x_norm, int64_t batch,
+                                        int64_t filters, int64_t spatial, const float *scales, const float *biases,
+                                        float *mean, float *variance, float *rolling_mean,
+                                        float *rolling_variance, int act, dnb_stream stream);
+/* dnb_bn_act_backward with sums over the whole data-parallel batch (normalize_delta divides
+ * by batch*spatial*world). Same rules as dnb_syncbn_act_forward_train. */
+dnb_status dnb_syncbn_act_backward(dnb_comm comm, const float *x, const float *y, const float *delta, float *dx,
+                                   int64_t batch, int64_t filters, int64_t spatial, const float *scales,
+                                   const float *biases, const float *mean, const float *variance,
+                                   float *bias_updates, float *scale_updates, float *mean_delta,
+                                   float *variance_delta, int act, dnb_stream stream);
 
 /* ------------------------------------------------------------------------------------ */
 /* sync-BN across GPUs (the reference has no multi-GPU support, README.md:313-317).        */
