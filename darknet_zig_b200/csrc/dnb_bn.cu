@@ -451,16 +451,16 @@ struct PArgs {
     unsigned *sync;           // [0] epoch, then 2 banks of {stats_done[kMaxGroups], apply_done[kMaxGroups]}
     unsigned *err, *abort_flag;
     unsigned long long wait_ns;
-    // sync-BN across GPUs (xon, any world >= 1): rank r's exchange buffer holds, for each launch
-    // parity, channel and source rank, one double2 record and one ready tag; xrec/xflag[r]
-    // point into rank r's buffer (a peer mapping, or this GPU's own buffer for r == rank)
+    // sync-BN across GPUs (xon, any world >= 1): every CTA stores its records of group g into
+    // every rank's buffer (xrec[r]: a peer mapping, or this GPU's own buffer for r == rank) and
+    // adds 1 to every rank's counter g (xcnt[r]); a rank has group g once its own counter
+    // passed xbase[g] + Ps * world
     int xon, world, rank;
-    unsigned xtag;            // this launch's tag (the communicator's call number)
-    int xpar;                 // xtag & 1: which half of the buffers this launch uses
-    int64_t xcmax;            // channels the buffers hold
-    double xcount;            // elements of one channel on one rank (batch*spatial)
-    double2 *xrec[kMaxRanks];
-    unsigned *xflag[kMaxRanks];
+    int xpar;                 // call number & 1: which half of the buffers this launch uses
+    int xpmax;                // CTAs a group's records have room for
+    unsigned xbase[kMaxSweepGroups];
+    float4 *xrec[kMaxRanks];
+    unsigned *xcnt[kMaxRanks];
 };
 
 // Share of CTA p of a role with `parts` CTAs in group g: units [t0, t1) of the group's T,
@@ -551,24 +551,25 @@ bool persistent_disabled() {
 }
 
 // Every CTA owns the same balanced share of each channel group in both passes, and its
-// warps are split in two. The 15 streaming warps reduce the groups (HBM reads) and write
+// warps are split by role. The 14 streaming warps reduce the groups (HBM reads) and write
 // the outputs of each group once its parameters are known (the share re-read from L2),
 // running `lag` groups of statistics ahead of the outputs; each warp walks its own chunks
 // and meets the others only through shared-memory counters, so one warp's phase change
-// never drains the whole CTA. The control warp polls two things: a group whose per-warp
-// partials are all in (it publishes the CTA's records and counts the CTA in
-// stats_done[g]), and the oldest published group that every CTA has counted itself in (it
+// never drains the whole CTA. The publisher warp takes a group's per-warp partials once
+// every streaming warp has counted itself, stores the CTA's records (with a communicator:
+// into every rank's buffer over NVLink) and counts the CTA in the group's counter with a
+// release-add; the merger warp waits until every CTA (of every rank) has counted itself,
 // merges the records of the share's channels and hands the apply parameters back through
-// shared memory). Publishing never waits behind a merge, so the exchanges of consecutive
-// groups overlap, and the grid-wide exchange (several L2 round trips behind saturated
-// memory pipes) stays off the streaming path. Statistics loads carry an L2 evict_last
-// policy, output-pass loads and stores evict_first, so a group stays in L2 between its two
-// passes. Every wait is bounded; on timeout the control warp sets the device error word
-// and tells the streaming warps to stop.
+// shared memory. A publish -- whose release waits for the record stores to land, a few
+// microseconds over NVLink -- never delays a merge, and the grid-wide exchange (several
+// L2 round trips behind saturated memory pipes) stays off the streaming path. Statistics
+// loads carry an L2 evict_last policy, output-pass loads and stores evict_first, so a group
+// stays in L2 between its two passes. Every wait is bounded; on timeout the merger sets the
+// device error word and tells the other warps to stop.
 
 constexpr int kSThreads = 512;              // threads of a sweep CTA
 constexpr int kSMinBlocks = 2;              // CTAs per SM the register budget is set for
-constexpr int kSWarps = kSThreads / 32 - 1;  // streaming warps; the last warp is the control warp
+constexpr int kSWarps = kSThreads / 32 - 2;  // streaming warps; then the publisher and the merger
 
 __device__ __forceinline__ uint64_t l2_evict_last() {
     uint64_t p;
@@ -592,7 +593,6 @@ __device__ __forceinline__ void st4_hint(float *p, float4 v, uint64_t pol) {
                  "f"(v.y), "f"(v.z), "f"(v.w), "l"(pol)
                  : "memory");
 }
-constexpr int kMaxSweepGroups = 16;
 
 template <bool BWD, int A, bool HASY>
 struct SweepKernel {
@@ -609,7 +609,7 @@ struct SweepKernel {
         double *lcnt;    // [G][2 segments] elements behind the forward's records
         int *done;       // [G] streaming warps that have left their partials of group g
         int *ready;      // [G] 1 once the parameters of group g are in ptab
-        int *stop;       // set by the control warp when a wait gave up
+        int *stop;       // set by the merger warp when a wait gave up
     };
     __host__ __device__ static size_t smem_bytes(int cap_units, int groups) {
         return (((size_t)groups * cap_units * sizeof(uint32_t) + 15) & ~(size_t)15) +
@@ -641,7 +641,7 @@ struct SweepKernel {
         return s;
     }
 
-    // Bounded spin of a whole warp until *flag >= want; false if the control warp stopped
+    // Bounded spin of a whole warp until *flag >= want; false if the merger warp stopped
     // the CTA or the wait gave up (the latter sets the device error word).
     __device__ static bool wait_smem(const PArgs &a, const Smem &s, const int *flag, int want) {
         const volatile int *f = flag;
@@ -788,7 +788,7 @@ struct SweepKernel {
         __syncwarp();
     }
 
-    // control warp: one record per segment from the streaming warps' partials of group g
+    // publisher warp: one record per segment from the streaming warps' partials of group g
     // (buffer b), written to a.rec; lane 0 then publishes them and counts the CTA
     __device__ static void publish(const PArgs &a, const Smem &s, int g, int rid, int b, unsigned *stats_done) {
         const Share sh = share_of(a, g, rid, a.f_ps);
@@ -810,33 +810,77 @@ struct SweepKernel {
                     q.y += __shfl_xor_sync(0xffffffffu, q.y, o);
                 }
             }
-            if (lane == 0) a.rec[((int64_t)g * a.Ps + rid) * 2 + j] = q;
+            if (a.xon) {
+                // lane r stores the record into rank r's buffer
+                if (lane < a.world)
+                    a.xrec[lane][xslot(a, g, a.rank, rid) + j] = q;
+            } else if (lane == 0) {
+                a.rec[((int64_t)g * a.Ps + rid) * 2 + j] = q;
+            }
         }
-        // lane 0 wrote every record: its release-add publishes them
-        if (lane == 0) asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(stats_done + g) : "memory");
+        // each storing lane's release-add publishes its records: lane 0 on this GPU, or
+        // lane r on rank r over NVLink
+        if (a.xon) {
+            if (lane < a.world)
+                asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(a.xcnt[lane] + a.xpar * kMaxSweepGroups + g)
+                             : "memory");
+        } else if (lane == 0) {
+            asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(stats_done + g) : "memory");
+        }
         __syncwarp();
     }
 
-    // control warp: merge this rank's records of the (at most two) channels of CTA rid's
-    // share of group g into s.lrec[g]; with a communicator, the CTA owning a channel's first
-    // unit then stores the merged record into every rank's exchange buffer over NVLink and
-    // tags it. Records of CTAs between the channel's first and last owner that hold no unit
-    // of it (a group with fewer units than CTAs) are skipped.
+    // index of CTA p's first record of group g from rank r in an exchange buffer
+    __device__ static size_t xslot(const PArgs &a, int g, int r, int p) {
+        return ((((size_t)a.xpar * kMaxSweepGroups + g) * a.world + r) * a.xpmax + p) * 2;
+    }
+
+    // merger warp: have all CTAs of every rank published group g? (lane 0's view)
+    __device__ static bool all_published(const PArgs &a, const unsigned *stats_done, int g) {
+        if (!a.xon) return ld_acquire_gpu(stats_done + g) >= (unsigned)a.Ps;
+        unsigned v;
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];"
+                     : "=r"(v)
+                     : "l"(a.xcnt[a.rank] + a.xpar * kMaxSweepGroups + g)
+                     : "memory");
+        return (int)(v - (a.xbase[g] + (unsigned)(a.Ps * a.world))) >= 0;
+    }
+
+    // merger warp: merge the records of the (at most two) channels of CTA rid's share of
+    // group g into s.lrec[g] -- this GPU's CTAs' records, or with a communicator every
+    // rank's, in the same order on every rank (so every rank gets the same statistics).
+    // Records of CTAs between the channel's first and last owner that hold no unit of it (a
+    // group with fewer units than CTAs) are skipped.
     __device__ static void merge_local(const PArgs &a, const Smem &s, int g, int rid) {
         const Share sh = share_of(a, g, rid, a.f_ps);
         const int lane = threadIdx.x & 31;
+        if (a.xon) {
+            // every lane acquires the counter lane 0 saw complete: orders its record loads
+            unsigned v;
+            asm volatile("ld.acquire.sys.global.u32 %0, [%1];"
+                         : "=r"(v)
+                         : "l"(a.xcnt[a.rank] + a.xpar * kMaxSweepGroups + g)
+                         : "memory");
+            (void)v;
+        }
         for (int j = 0; j < sh.nseg; ++j) {
             const int cl = sh.cfirst + j;
-            const int64_t c = (int64_t)sh.c0 + cl;
             const uint32_t ua = (uint32_t)cl * a.NK, ub = ua + a.NK;
             const int plo = owner_of(a, g, ua, a.Ps), phi = owner_of(a, g, ub - 1, a.Ps);
-            const int nrec = phi - plo + 1;
+            const int per_rank = phi - plo + 1;
+            const int nrec = a.xon ? per_rank * a.world : per_rank;
             auto load = [&](int idx, float4 &dst) -> bool {
-                const int p = plo + idx;
+                int q = 0, k = idx;
+                if (a.xon) {
+                    q = idx / per_rank;
+                    k = idx - q * per_rank;
+                }
+                const int p = plo + k;
                 const Share o = share_of(a, g, p, a.f_ps);
                 const uint32_t lo = ua > o.t0 ? ua : o.t0, hi = ub < o.t1 ? ub : o.t1;
                 if (hi <= lo) return false;
-                dst = __ldcg(&a.rec[((int64_t)g * a.Ps + p) * 2 + (cl - o.cfirst)]);
+                dst = a.xon ? __ldcg(&a.xrec[a.rank][xslot(a, g, q, p) + (cl - o.cfirst)])
+                            : __ldcg(&a.rec[((int64_t)g * a.Ps + p) * 2 + (cl - o.cfirst)]);
                 return true;
             };
             constexpr int R = 2;  // records held per lane: one L2 round trip up to 64 records
@@ -897,41 +941,13 @@ struct SweepKernel {
                 mine = make_double2(warp_sum(s1), warp_sum(s2));
             }
             if (lane == 0) s.lrec[2 * g + j] = mine;
-            if (a.xon && plo == rid && lane < a.world) {
-                // this CTA owns the channel's first unit: send the record to rank `lane`
-                const size_t slot = ((size_t)a.xpar * a.xcmax + c) * a.world + a.rank;
-                asm volatile("st.global.v2.f64 [%0], {%1, %2};" ::"l"(a.xrec[lane] + slot), "d"(mine.x),
-                             "d"(mine.y)
-                             : "memory");
-                asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a.xflag[lane] + slot), "r"(a.xtag)
-                             : "memory");
-            }
         }
         __syncwarp();
     }
 
-    // control warp, with a communicator: have every rank's records of the channels of CTA
-    // rid's share of group g arrived in this GPU's buffer? (warp-uniform; acquires them)
-    __device__ static bool peers_ready(const PArgs &a, int g, int rid) {
-        const Share sh = share_of(a, g, rid, a.f_ps);
-        const int lane = threadIdx.x & 31;
-        bool ok = true;
-        for (int j = 0; j < sh.nseg; ++j) {
-            if (lane < a.world) {
-                const int64_t c = (int64_t)sh.c0 + sh.cfirst + j;
-                const unsigned *flag = a.xflag[a.rank] + ((size_t)a.xpar * a.xcmax + c) * a.world + lane;
-                unsigned v;
-                asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
-                ok = ok && v == a.xtag;
-            }
-        }
-        return __all_sync(0xffffffffu, ok) != 0;
-    }
-
-    // control warp: the statistics of the channels of CTA rid's share of group g -- this
-    // rank's merged records, combined in rank order with the other ranks' (same order,
-    // same result on every rank) -- closed into the apply parameters s.ptab[g]; the CTA
-    // owning a channel's first unit writes the per-channel outputs.
+    // merger warp: the merged statistics of the channels of CTA rid's share of group g
+    // closed into the apply parameters s.ptab[g]; the CTA owning a channel's first unit
+    // writes the per-channel outputs.
     __device__ static void finalize(const PArgs &a, const Smem &s, int g, int rid) {
         const Share sh = share_of(a, g, rid, a.f_ps);
         const int lane = threadIdx.x & 31;
@@ -940,29 +956,8 @@ struct SweepKernel {
             const int64_t c = (int64_t)sh.c0 + cl;
             const uint32_t ua = (uint32_t)cl * a.NK;
             const bool write = owner_of(a, g, ua, a.Ps) == rid;
-            double2 tot = s.lrec[2 * g + j];
-            double n = s.lcnt[2 * g + j];
-            if (a.xon) {
-                double2 r2 = make_double2(0.0, 0.0);
-                const bool in = lane < a.world;
-                if (in) {
-                    const double2 *src = a.xrec[a.rank] + ((size_t)a.xpar * a.xcmax + c) * a.world + lane;
-                    asm volatile("ld.relaxed.sys.global.v2.f64 {%0, %1}, [%2];"
-                                 : "=d"(r2.x), "=d"(r2.y)
-                                 : "l"(src)
-                                 : "memory");
-                }
-                if constexpr (!BWD) {
-                    // every rank holds a.xcount elements of the channel: Chan's merge of the
-                    // ranks' (mean, M2), lanes in rank order
-                    n = a.xcount * a.world;
-                    const double mu = warp_sum(in ? r2.x : 0.0) / a.world;
-                    const double d = in ? r2.x - mu : 0.0;
-                    tot = make_double2(mu, warp_sum(in ? r2.y + a.xcount * d * d : 0.0));
-                } else {
-                    tot = make_double2(warp_sum(in ? r2.x : 0.0), warp_sum(in ? r2.y : 0.0));
-                }
-            }
+            const double2 tot = s.lrec[2 * g + j];
+            const double n = s.lcnt[2 * g + j];
             if (lane == 0) {
                 float *out = s.ptab + (2 * g + j) * 8;
                 const float gamma = a.scales[c], beta = a.biases[c];
@@ -1071,66 +1066,53 @@ __global__ void __launch_bounds__(kSThreads, kSMinBlocks) k_bn_sweep(PArgs a) {
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     if (warp == kSWarps) {
-        // control warp
+        // publisher: groups in order, as soon as every streaming warp's partials are in
         if (rid == 0) {  // the next launch's bank
             unsigned *other = a.sync + 1 + (size_t)((epoch & 1u) ^ 1u) * 2 * kMaxGroups;
             for (int i = lane; i < 2 * kMaxGroups; i += 32) other[i] = 0u;
         }
-        // groups move through: published (pub) -> merged on this rank and, with a
-        // communicator, sent to the other ranks (loc) -> finalised, parameters in shared
-        // memory (fin); no step waits behind another group's
-        int pub = 0, loc = 0, fin = 0;
-        unsigned long long deadline = global_ns() + a.wait_ns;
-        bool ok = true;
-        while (fin < a.G) {
-            int what = 0;  // 1: publish group pub, 2: finalise group fin, 3: merge group loc
-            if (lane == 0) {
-                if (pub < a.G && *reinterpret_cast<volatile int *>(&s.done[pub]) >= kSWarps) what = 1;
-                else if (loc < pub && ld_acquire_gpu(stats_done + loc) >= (unsigned)a.Ps) what = 3;
-            }
-            what = __shfl_sync(0xffffffffu, what, 0);
-            if (what == 0 && a.xon && fin < loc && K::peers_ready(a, fin, rid)) what = 2;
-            if (what == 0 && lane == 0) {
-                if (ld_volatile(a.abort_flag)) what = 4;
-                else if (global_ns() > deadline) {
-                    atomicOr(a.err, fin < loc ? DEVERR_WAIT_PEER : DEVERR_WAIT_BARRIER);
-                    atomicExch(a.abort_flag, 1u);
-                    what = 4;
-                }
-            }
-            what = __shfl_sync(0xffffffffu, what, 0);
-            __syncwarp();  // lane 0's checks order the other lanes' reads
-            if (what == 4) {
-                ok = false;
-                break;
-            }
-            if (what == 0) {
-                __nanosleep(32);
-                continue;
-            }
-            if (what == 1) {
-                __threadfence_block();
-                K::publish(a, s, pub, rid, pub, stats_done);
-                ++pub;
-            } else if (what == 3) {
-                // every CTA has read the epoch once all have counted themselves in group 0
-                if (loc == 0 && rid == 0 && lane == 0) atomicExch(&a.sync[0], epoch + 1);
-                K::merge_local(a, s, loc, rid);
-                ++loc;
-                if (!a.xon) what = 2;  // nothing to wait for
-            }
-            if (what == 2) {
-                K::finalize(a, s, fin, rid);
-                if (lane == 0) {
-                    __threadfence_block();
-                    *reinterpret_cast<volatile int *>(&s.ready[fin]) = 1;
-                }
-                __syncwarp();
-                ++fin;
-            }
-            deadline = global_ns() + a.wait_ns;
+        for (int g = 0; g < a.G; ++g) {
+            if (!K::wait_smem(a, s, &s.done[g], kSWarps)) return;
+            K::publish(a, s, g, rid, g, stats_done);
         }
-        if (!ok && lane == 0) *reinterpret_cast<volatile int *>(s.stop) = 1;
+        return;
+    }
+    if (warp == kSWarps + 1) {
+        // merger: groups in order, once every CTA (of every rank) has published
+        for (int g = 0; g < a.G; ++g) {
+            int ok = 1;
+            if (lane == 0) {
+                const unsigned long long deadline = global_ns() + a.wait_ns;
+                while (!K::all_published(a, stats_done, g)) {
+                    if (ld_volatile(a.abort_flag)) {
+                        ok = 0;
+                        break;
+                    }
+                    if (global_ns() > deadline) {
+                        atomicOr(a.err, a.xon ? DEVERR_WAIT_PEER : DEVERR_WAIT_BARRIER);
+                        atomicExch(a.abort_flag, 1u);
+                        ok = 0;
+                        break;
+                    }
+                    __nanosleep(32);
+                }
+            }
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            __syncwarp();  // lane 0's acquire orders the other lanes' record loads
+            if (!ok) {
+                if (lane == 0) *reinterpret_cast<volatile int *>(s.stop) = 1;
+                return;
+            }
+            // every CTA has read the epoch once all have counted themselves in group 0
+            if (g == 0 && rid == 0 && lane == 0) atomicExch(&a.sync[0], epoch + 1);
+            K::merge_local(a, s, g, rid);
+            K::finalize(a, s, g, rid);
+            if (lane == 0) {
+                __threadfence_block();
+                *reinterpret_cast<volatile int *>(&s.ready[g]) = 1;
+            }
+            __syncwarp();
+        }
         return;
     }
     // streaming warps: statistics of groups 0 .. lag-1, then per group g the statistics of
@@ -1264,16 +1246,17 @@ dnb_status run_sweep(int64_t batch, int64_t filters, int64_t spatial, int act, P
         a.xon = 0;
         a.world = 1;
         if (cv) {
+            if (pl.P > cv->pmax || pl.G > kMaxSweepGroups)
+                return fail(DNB_ERR_UNSUPPORTED, "%s: plan exceeds the communicator's buffers", what);
             a.xon = 1;
             a.world = cv->world;
             a.rank = cv->rank;
-            a.xtag = cv->tag;
             a.xpar = (int)(cv->tag & 1u);
-            a.xcmax = cv->cmax;
-            a.xcount = (double)(batch * spatial);
+            a.xpmax = cv->pmax;
+            for (int g = 0; g < kMaxSweepGroups; ++g) a.xbase[g] = cv->base[g];
             for (int r = 0; r < cv->world; ++r) {
-                a.xrec[r] = static_cast<double2 *>(cv->rec[r]);
-                a.xflag[r] = cv->flag[r];
+                a.xrec[r] = cv->rec[r];
+                a.xcnt[r] = cv->cnt[r];
             }
             // normalize_delta divides by the element count of the whole batch
             a.denom = (float)(batch * spatial * cv->world);
@@ -1293,6 +1276,8 @@ dnb_status run_sweep(int64_t batch, int64_t filters, int64_t spatial, int act, P
         cfg.numAttrs = 1;
         DNB_CUDA(cudaLaunchKernelEx(&cfg, kern, a));
         *launched = true;
+        if (cv)  // every CTA of every rank adds 1 to each counter of the groups this launch uses
+            for (int g = 0; g < pl.G; ++g) cv->base[g] += (unsigned)(pl.P * cv->world);
         return after_launch(stream, what);
     });
 }

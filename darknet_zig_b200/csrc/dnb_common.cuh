@@ -64,15 +64,20 @@ struct Workspace {
 constexpr int kMaxGroups = 1024;
 constexpr size_t kSyncWords = 1 + 4 * (size_t)kMaxGroups;
 
-// A sync-BN communicator as a kernel sees it (dnb_comm.cu): this rank, the ranks, the call
-// number of the launch and every rank's exchange buffer (records, then ready tags).
+// A sync-BN communicator as a kernel sees it (dnb_comm.cu): this rank, the ranks, and every
+// rank's exchange buffer: records float4 [2 parities][kMaxSweepGroups][world][pmax CTAs][2]
+// and arrival counters u32 [2 parities][kMaxSweepGroups]. Counters only grow; base[g] is
+// what counter g of this launch's parity held before the launch (the host keeps it).
 constexpr int kMaxRanks = 8;
+constexpr int kMaxSweepGroups = 16;
 struct CommView {
     int rank = 0, world = 1;
-    unsigned tag = 0;
+    unsigned tag = 0;  // the call number; parity = tag & 1
+    int pmax = 0;      // CTAs a group's records have room for
     int64_t cmax = 0;
-    void *rec[kMaxRanks] = {};
-    unsigned *flag[kMaxRanks] = {};
+    float4 *rec[kMaxRanks] = {};
+    unsigned *cnt[kMaxRanks] = {};
+    unsigned *base = nullptr;  // host: [kMaxSweepGroups] counters' values before this launch
 };
 // The view of `comm` for its next fused call on the current device (advances its call number).
 dnb_status comm_next(dnb_comm comm, CommView *out);
