@@ -69,6 +69,10 @@ def parse():
     ap.add_argument("--syncbn", choices=["fused", "split"], default="fused",
                     help="N > 1: statistics exchanged inside the fused kernels over NVLink (fused) or by "
                          "NCCL collectives between split kernels (split)")
+    ap.add_argument("--ops", action="store_true",
+                    help="instead of the step: time every other op of the path at its BASELINE config shape, "
+                         "one JSON line per op")
+    ap.add_argument("--op", default="", help="with --ops: only the ops whose name contains this")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     a = ap.parse_args()
@@ -507,8 +511,115 @@ def run_reference(a):
     print(json.dumps(line), flush=True)
 
 
+# ---- the other ops of the path -----------------------------------------------------------
+
+def run_ops(a):
+    """Device time of every other op at its BASELINE config shape (1 GPU): back-to-back
+    launches over rotating buffer sets larger than L2 together, CUDA events around them;
+    GB/s = algorithmic bytes (each tensor read or written once) / time."""
+    import torch
+
+    from darknet_zig_b200 import gpu
+
+    torch.cuda.set_device(0)
+    gpu.init(0)
+    peak, _ = measured_peaks()
+    stream = torch.cuda.current_stream()
+    steps = max(a.steps, 10)
+
+    def timed(name, config, nbytes, make, run):
+        if a.op and a.op not in name:
+            return
+        n_sets = int(min(8, max(2, -(-(3 * 126 * 2**20) // max(nbytes, 1)) + 1)))
+        sets = [make(i) for i in range(n_sets)]
+        for k in range(a.warmup):
+            run(sets[k % n_sets])
+        torch.cuda.synchronize()
+        torch.cuda._sleep(int(0.1e-3 * 2e9) * steps)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for k in range(steps):
+            run(sets[k % n_sets])
+        e1.record(stream)
+        torch.cuda.synchronize()
+        gpu.check_device_error()
+        us = e0.elapsed_time(e1) / steps * 1e3
+        gbs = nbytes / (us * 1e-6) / 1e9
+        print(json.dumps({"op": name, "config": config, "us": round(us, 2), "GBps": round(gbs, 1),
+                          "frac_of_peak": round(gbs / peak, 4), "algorithmic_bytes": int(nbytes),
+                          "rotating_sets": n_sets}), flush=True)
+
+    f32 = dict(dtype=torch.float32, device="cuda")
+    LEAKY_ = LEAKY
+    # cfg2: inference BN + leaky over the tiny-classifier stack, N=64; maxpool 2x2/s2 between stages
+    stack = [(16, 224), (32, 112), (64, 56), (128, 28), (256, 14), (512, 7), (1024, 7)]
+    for c, hw in stack:
+        E = 64 * c * hw * hw
+
+        def make_bn(i, E=E, c=c):
+            return (torch.randn(E, **f32), torch.empty(E, **f32), torch.rand(c, **f32) + 0.5, torch.randn(c, **f32),
+                    torch.randn(c, **f32), torch.rand(c, **f32) + 0.5)
+
+        timed("bn_act_forward_infer", f"cfg2 64x{c}x{hw}x{hw} leaky", 8 * E, make_bn,
+              lambda t, c=c, hw=hw: gpu.bnActForwardInfer(t[0], t[1], 64, c, hw * hw, t[2], t[3], t[4], t[5], LEAKY_))
+    for c, hw in stack[:5]:
+        E = 64 * c * hw * hw
+        On = E // 4
+
+        def make_mp(i, E=E, On=On):
+            return (torch.randn(E, **f32), torch.empty(On, **f32), torch.empty(On, dtype=torch.int32, device="cuda"))
+
+        timed("forward_maxpool", f"cfg2 64x{c}x{hw}x{hw} 2x2/s2 with indices", 4 * E + 8 * On, make_mp,
+              lambda t, c=c, hw=hw, On=On: gpu.forwardMaxpool(On, hw, hw, c, 2, 2, 1, t[0], t[1], t[2]))
+    # cfg3: classifier head at N=256
+    E = 256 * 1000 * 49
+    timed("forward_avgpool", "cfg3 256x1000x7x7", 4 * E + 4 * 256 * 1000,
+          lambda i: (torch.randn(E, **f32) * 2, torch.empty(256 * 1000, **f32)),
+          lambda t: gpu.forwardAvgpool(256 * 1000, 7, 7, 1000, t[0], t[1]))
+
+    def make_sx(i):
+        truth = torch.zeros(256, 1000, **f32)
+        truth[torch.arange(256), torch.randint(0, 1000, (256,))] = 1.0
+        return (torch.randn(256 * 1000, **f32), truth.view(-1), torch.empty(256 * 1000, **f32),
+                torch.empty(256 * 1000, **f32), torch.empty(256 * 1000, **f32), torch.zeros(1, **f32))
+
+    timed("softmax_xent", "cfg3 256 rows x 1000 classes", 16 * 256 * 1000, make_sx,
+          lambda t: gpu.softmaxXent(t[0], t[1], 1000, 256, 1.0, t[2], t[3], t[4], t[5]))
+    E = 256 * 512 * 196
+    timed("shortcut", "cfg3 256x512x14x14 + same shape", 12 * E,
+          lambda i: (torch.randn(E, **f32), torch.randn(E, **f32)),
+          lambda t: gpu.shortcut(256, 14, 14, 512, t[0], 14, 14, 512, 1.0, 1.0, t[1]))
+    # cfg4: SGD momentum on the 64 Mi weight vector; BN + leaky per GPU at 128x256x28x28
+    n = 64 << 20
+    timed("sgd_momentum", "cfg4 64 Mi weights, lr 0.1 momentum 0.9 decay 5e-4 batch 1024", 16 * n,
+          lambda i: (torch.randn(n, **f32) * 0.01, torch.randn(n, **f32) * 1e-3),
+          lambda t: gpu.sgdMomentum(n, t[0], t[1], 0.1, 0.9, 5e-4, 1024))
+    E = 128 * 256 * 784
+
+    def make_bnt(i):
+        return (torch.randn(E, **f32), torch.empty(E, **f32), torch.randn(E, **f32), torch.empty(E, **f32),
+                torch.rand(256, **f32) + 0.5, torch.randn(256, **f32) * 0.1,
+                *(torch.zeros(256, **f32) for _ in range(8)))
+
+    timed("bn_act_forward_train", "cfg4 per GPU 128x256x28x28 leaky", 8 * E, make_bnt,
+          lambda t: gpu.bnActForwardTrain(t[0], t[1], None, 128, 256, 784, t[4], t[5], t[6], t[7], t[8], t[9],
+                                          LEAKY_))
+    timed("bn_act_backward", "cfg4 per GPU 128x256x28x28 leaky", 12 * E, make_bnt,
+          lambda t: gpu.bnActBackward(t[0], None, t[2], t[3], 128, 256, 784, t[4], t[5], t[6], t[7], t[10], t[11],
+                                      t[12], t[13], LEAKY_))
+    # the BLAS-1 basics on 64 Mi floats
+    timed("fill", "64 Mi floats", 4 * n, lambda i: (torch.empty(n, **f32),), lambda t: gpu.fill(t[0], n, 0.5))
+    timed("copy", "64 Mi floats", 8 * n, lambda i: (torch.randn(n, **f32), torch.empty(n, **f32)),
+          lambda t: gpu.copy(n, t[0], t[1]))
+    timed("axpy", "64 Mi floats", 12 * n, lambda i: (torch.randn(n, **f32), torch.randn(n, **f32)),
+          lambda t: gpu.axpy(n, 0.5, t[0], t[1]))
+
+
 def main():
     a = parse()
+    if a.ops:
+        run_ops(a)
+        return
     if a.impl == "reference":
         run_reference(a)
     else:

@@ -60,6 +60,49 @@ __global__ void __launch_bounds__(kThreads) k_maxpool_fwd(int64_t out_n, int in_
     }
 }
 
+// The darknet default 2x2 / stride 2 window (pad 1, so offset 0) on even images: every tap
+// is inside the image, and two adjacent outputs read one 16-byte run of each of their two
+// input rows. One thread per output pair; the taps are compared in the generic kernel's
+// (row, col) order with the same strict '>', so values and indices are identical to it.
+__global__ void __launch_bounds__(kThreads) k_maxpool_2x2(int64_t pairs, int in_w, int out_w, FastDiv fpw,
+                                                          FastDiv foh, const float *__restrict__ in,
+                                                          float *__restrict__ out, int32_t *__restrict__ idx) {
+    const int64_t step = (int64_t)gridDim.x * kThreads;
+    for (int64_t id = (int64_t)blockIdx.x * kThreads + threadIdx.x; id < pairs; id += step) {
+        uint32_t t, jp, q, i;
+        fpw.divmod((uint32_t)id, t, jp);
+        foh.divmod(t, q, i);
+        const int64_t row0 = ((int64_t)q * (2 * foh.d) + 2 * i) * in_w + 4 * (int64_t)jp;
+        const int64_t row1 = row0 + in_w;
+        const float4 a = ld4(in + row0), b = ld4(in + row1);
+        float2 best;
+        int2 bi;
+        {  // output 2 jp: taps (row0, 0), (row0, 1), (row1, 0), (row1, 1)
+            float v = -FLT_MAX;
+            int k = -1;
+            if (a.x > v) { v = a.x; k = (int)row0; }
+            if (a.y > v) { v = a.y; k = (int)row0 + 1; }
+            if (b.x > v) { v = b.x; k = (int)row1; }
+            if (b.y > v) { v = b.y; k = (int)row1 + 1; }
+            best.x = v;
+            bi.x = k;
+        }
+        {  // output 2 jp + 1
+            float v = -FLT_MAX;
+            int k = -1;
+            if (a.z > v) { v = a.z; k = (int)row0 + 2; }
+            if (a.w > v) { v = a.w; k = (int)row0 + 3; }
+            if (b.z > v) { v = b.z; k = (int)row1 + 2; }
+            if (b.w > v) { v = b.w; k = (int)row1 + 3; }
+            best.y = v;
+            bi.y = k;
+        }
+        const int64_t o = (int64_t)t * out_w + 2 * (int64_t)jp;
+        *reinterpret_cast<float2 *>(out + o) = best;
+        *reinterpret_cast<int2 *>(idx + o) = bi;
+    }
+}
+
 __device__ __forceinline__ int ceil_div_pos(int a, int b) { return a >= 0 ? (a + b - 1) / b : a / b; }
 
 // pooling.zig:95-103 as a gather: input element `in` receives, in increasing output index,
@@ -160,7 +203,14 @@ dnb_status dnb_forward_maxpool(int64_t out_n, int64_t in_h, int64_t in_w, int64_
     const FastDiv fw((uint32_t)out_w), fh((uint32_t)out_h);
     const int off = -(int)(pad / 2);
     const unsigned grid = grid_for(out_n, kThreads, ds);
-    if (size == 2)
+    if (size == 2 && stride == 2 && off == 0 && in_h == 2 * out_h && in_w == 2 * out_w && in_w % 4 == 0 && fast &&
+        aligned16(input) && (reinterpret_cast<uintptr_t>(output) & 7u) == 0 &&
+        (reinterpret_cast<uintptr_t>(indexes) & 7u) == 0) {
+        const int64_t pairs = out_n / 2;
+        k_maxpool_2x2<<<grid_for(pairs, kThreads, ds), kThreads, 0, s>>>(
+            pairs, (int)in_w, (int)out_w, FastDiv((uint32_t)(out_w / 2)), FastDiv((uint32_t)out_h), input, output,
+            indexes);
+    } else if (size == 2)
         k_maxpool_fwd<2><<<grid, kThreads, 0, s>>>(out_n, (int)in_h, (int)in_w, (int)out_h, (int)out_w, (int)stride, 2,
                                                    off, fw, fh, fast, input, output, indexes);
     else if (size == 3)

@@ -81,6 +81,74 @@ __global__ void __launch_bounds__(kThreads) k_softmax_xent(const float *in, cons
     }
 }
 
+// misc.zig:41-50 fused, one block per row with the row staged in shared memory (rows of up
+// to kRowSmem floats): the row is read from HBM once, the max and the sum are block trees,
+// and output, err and delta are written in one pass. A classifier head has few rows (256 at
+// BASELINE config 3), so a warp per row leaves most of the GPU idle and walks each row
+// three times through global memory; a block per row reads 1000 classes in 4 loads a thread.
+constexpr int kRowSmem = 12288;  // floats of one staged row (48 KB)
+
+__device__ __forceinline__ float block_max(float v, float *red) {
+    v = warp_max(v);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float t = threadIdx.x < kWarps ? red[threadIdx.x] : -FLT_MAX;
+    if (threadIdx.x < 32) t = warp_max(t);
+    if (threadIdx.x == 0) red[kWarps] = t;
+    __syncthreads();
+    t = red[kWarps];
+    __syncthreads();
+    return t;
+}
+__device__ __forceinline__ float block_sum_f(float v, float *red) {
+    v = warp_sum(v);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float t = threadIdx.x < kWarps ? red[threadIdx.x] : 0.0f;
+    if (threadIdx.x < 32) t = warp_sum(t);
+    if (threadIdx.x == 0) red[kWarps] = t;
+    __syncthreads();
+    t = red[kWarps];
+    __syncthreads();
+    return t;
+}
+
+__global__ void __launch_bounds__(kThreads) k_softmax_xent_rows(const float *in, const float *truth, int64_t n,
+                                                                int64_t batch, float temp, float *out, float *delta,
+                                                                float *err, float *row_loss) {
+    extern __shared__ float row[];
+    __shared__ float red[kWarps + 1];
+    for (int64_t q = blockIdx.x; q < batch; q += gridDim.x) {
+        const int64_t off = q * n;
+        float largest = -FLT_MAX;  // blas.zig:214
+        for (int64_t i = threadIdx.x; i < n; i += kThreads) {
+            const float v = in[off + i];
+            row[i] = v;
+            largest = v > largest ? v : largest;
+        }
+        largest = block_max(largest, red);
+        float sum = 0.0f;
+        for (int64_t i = threadIdx.x; i < n; i += kThreads) {
+            const float e = expf(row[i] / temp - largest / temp);  // blas.zig:218
+            row[i] = e;
+            sum += e;
+        }
+        sum = block_sum_f(sum, red);
+        float loss = 0.0f;
+        for (int64_t i = threadIdx.x; i < n; i += kThreads) {
+            const float p = row[i] / sum;  // blas.zig:221
+            const float t = truth[off + i];
+            const float e = t != 0.0f ? -logf(p) : 0.0f;  // blas.zig:250
+            out[off + i] = p;
+            err[off + i] = e;
+            delta[off + i] = t - p;  // blas.zig:251
+            loss += e;
+        }
+        loss = block_sum_f(loss, red);
+        if (threadIdx.x == 0 && row_loss) row_loss[q] = loss;
+    }
+}
+
 // The cost: rows added in fp64 in row order by one block (deterministic).
 __global__ void k_cost(const float *row_loss, int64_t batch, float *cost) {
     __shared__ double part[32];
@@ -150,8 +218,20 @@ dnb_status dnb_softmax_xent(const float *input, const float *truth, int64_t n, i
         DNB_TRY(workspace(s, sizeof(float) * (size_t)batch, &ws));
         row_loss = static_cast<float *>(ws->scratch);
     }
-    k_softmax_xent<<<rows_grid(batch, ds), kThreads, 0, s>>>(input, truth, n, batch, temp, output, delta, err,
-                                                             row_loss);
+    if (n <= kRowSmem) {
+        static size_t smem_set = 0;
+        const size_t smem = sizeof(float) * (size_t)n;
+        if (smem > 48 * 1024 && smem > smem_set) {
+            DNB_CUDA(cudaFuncSetAttribute(k_softmax_xent_rows, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+            smem_set = smem;
+        }
+        const int64_t cap = (int64_t)ds->sm_count * 8;
+        const unsigned grid = (unsigned)(batch < cap ? batch : cap);
+        k_softmax_xent_rows<<<grid, kThreads, smem, s>>>(input, truth, n, batch, temp, output, delta, err, row_loss);
+    } else {
+        k_softmax_xent<<<rows_grid(batch, ds), kThreads, 0, s>>>(input, truth, n, batch, temp, output, delta, err,
+                                                                 row_loss);
+    }
     DNB_TRY(after_launch(s, "softmax_xent"));
     if (cost) {
         k_cost<<<1, 1024, 0, s>>>(row_loss, batch, cost);

@@ -128,6 +128,22 @@ MAXPOOL_CASES = [
 ]
 
 
+def test_maxpool_2x2_ties_keep_the_first_maximum(cuda, oracle):
+    """The vectorised 2x2 / stride-2 path with many equal values: the first maximum in
+    (row, col) tap order wins, as in pooling.zig:59-93."""
+    B, C, H, W = 2, 4, 8, 16
+    x = np.round(synth.uniform(23, (B * C * H * W,), -1, 1) * 2).astype(np.float32) / 2
+    oh, ow = H // 2, W // 2
+    out = torch.empty(B * C * oh * ow, dtype=torch.float32, device="cuda")
+    idx = torch.empty(B * C * oh * ow, dtype=torch.int32, device="cuda")
+    gpu.forwardMaxpool(B * C * oh * ow, H, W, C, 2, 2, 1, dev(x), out, idx)
+    w_out = np.zeros(B * C * oh * ow, np.float32)
+    w_idx = np.zeros(B * C * oh * ow, np.int32)
+    oracle.forward_maxpool(B, H, W, C, 2, 2, 1, x, w_out, w_idx)
+    assert_bitexact(host(out), w_out, "maxpool values")
+    assert (host(idx) == w_idx).all(), "maxpool indices differ"
+
+
 @pytest.mark.parametrize("case", MAXPOOL_CASES)
 def test_maxpool_bitexact(cuda, oracle, case):
     B, C, H, W, size, stride, pad = case
@@ -175,7 +191,7 @@ def test_avgpool(cuda, oracle, case):
     assert_bitexact(host(ind), w, "avgpool backward")
 
 
-@pytest.mark.parametrize("rows,classes", [(8, 137), (256, 1000), (3, 5000), (1, 1)])
+@pytest.mark.parametrize("rows,classes", [(8, 137), (256, 1000), (3, 5000), (1, 1), (2, 13001)])
 def test_softmax_and_cross_entropy(cuda, oracle, rows, classes):
     n = rows * classes
     x = synth.normal(19, (n,), 0, 2)
