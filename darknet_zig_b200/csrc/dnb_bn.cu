@@ -811,6 +811,12 @@ struct SweepKernel {
                 }
             }
             if (a.xon) {
+                // the butterfly leaves lanes with values that differ in the last bits (Chan's
+                // merge is not symmetric): every rank must get lane 0's record
+                q.x = __shfl_sync(0xffffffffu, q.x, 0);
+                q.y = __shfl_sync(0xffffffffu, q.y, 0);
+                q.z = __shfl_sync(0xffffffffu, q.z, 0);
+                q.w = __shfl_sync(0xffffffffu, q.w, 0);
                 // lane r stores the record into rank r's buffer
                 if (lane < a.world)
                     a.xrec[lane][xslot(a, g, a.rank, rid) + j] = q;
