@@ -30,7 +30,11 @@ from pinned memory and y and dx copied out every step, inside the timed region.
 
 `--impl reference` times the reference's CPU implementation of the same step (the C
 restatement of blas.zig / batchnorm.zig / activations.zig in oracle/, the reference's own
-Zig code having no toolchain here) on all host cores.
+Zig code having no toolchain here) on all host cores. Where a GPU and the reference's own
+kernel file built for sm_100a (oracle/_ref/libref_gpu.so) are present, its line also carries
+`gpu_kernels`: the reference's unfused GPU layer sequences (12 launches forward, 7 backward,
+with the reference's grids) timed on the same workload the same way as this library's step,
+and its 3-launch SGD weight update on 64 Mi weights.
 """
 from __future__ import annotations
 
@@ -478,12 +482,107 @@ def cpu_baseline(a, threads):
             "ms_per_step": round(t * 1e3, 2), "elems_per_s": round(E / t, 1)}
 
 
+def ref_gpu_kernels(a):
+    """The reference's GPU path on this box's GPU 0: darknet_kernels.hip compiled for sm_100a
+    with the reference's flags, launched with the reference's grids (oracle/ref_gpu.cu). One
+    step = the conv-layer BN + leaky forward sequence (convolutional.zig:263-268,
+    batchnorm.zig:129-153) and backward sequence (convolutional.zig:279-282,
+    batchnorm.zig:155-170). Timed like this library's step: rotating tensor sets larger than
+    L2 together, K back-to-back steps between one pair of events after W warm-up steps.
+    Returns None when there is no GPU or the library was not built."""
+    try:
+        import torch
+    except ImportError:
+        return None
+    if not torch.cuda.is_available():
+        return None
+    try:
+        from oracle.oracle import RefGpu
+
+        ref = RefGpu()
+    except (FileNotFoundError, OSError) as e:
+        return {"unavailable": f"reference kernel library: {e}"}
+    torch.cuda.set_device(0)
+    B, C, H, W = a.shape
+    S = H * W
+    E = B * C * S
+    g = torch.Generator(device="cuda")
+    g.manual_seed(4321)
+    # per set: the conv output (forward in place), the saved x and x_norm, delta (backward in place)
+    n_sets = max(2, -(-(3 * 126 * 2**20) // (4 * E * 4)) + 1)
+    sets = [tuple(torch.randn(E, generator=g, device="cuda") for _ in range(4)) for _ in range(n_sets)]
+    gamma = torch.rand(C, generator=g, device="cuda") + 0.5
+    beta = torch.randn(C, generator=g, device="cuda") * 0.1
+    mean, var, rm, rv, bu, su, md, vd = (torch.zeros(C, device="cuda") for _ in range(8))
+    stream = torch.cuda.current_stream()
+    sh = stream.cuda_stream
+    P = lambda t: t.data_ptr()  # noqa: E731
+
+    def fwd(k):
+        out, xs, xn, _ = sets[k % n_sets]
+        ref.conv_bn_forward(P(out), P(xs), P(xn), P(mean), P(var), P(rm), P(rv), P(gamma), P(beta), B, C, S,
+                            LEAKY, sh)
+
+    def bwd(k):
+        out, xs, xn, delta = sets[(k + 1) % n_sets]
+        ref.conv_bn_backward(P(out), P(delta), P(xs), P(xn), P(mean), P(var), P(gamma), P(bu), P(su), P(md), P(vd),
+                             B, C, S, LEAKY, sh)
+
+    def timed(body, steps):
+        torch.cuda.synchronize()
+        torch.cuda._sleep(int(2e-3 * 2e9) * max(1, steps // 4))
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for k in range(steps):
+            body(k)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / steps
+
+    for k in range(a.warmup):
+        fwd(k)
+        bwd(k)
+    torch.cuda.synchronize()
+    ms_step = timed(lambda k: (fwd(k), bwd(k)), a.steps)
+    ms_fwd = timed(fwd, a.steps)
+    ms_bwd = timed(bwd, a.steps)
+    del sets
+    # SGD weight update of BASELINE config 4: 64 Mi weights, 3 launches (axpy, axpy, scal)
+    nw = 64 << 20
+    wsets = [(torch.randn(nw, generator=g, device="cuda") * 0.01, torch.randn(nw, generator=g, device="cuda") * 1e-3)
+             for _ in range(2)]
+
+    def sgd(k):
+        w, wu = wsets[k % 2]
+        ref.sgd_weights(nw, 0.1, 0.9, 5e-4, 1024, P(w), P(wu), sh)
+
+    for k in range(a.warmup):
+        sgd(k)
+    ms_sgd = timed(sgd, a.steps)
+    del wsets
+    torch.cuda.empty_cache()
+    gbs = lambda nbytes, ms: round(nbytes / (ms * 1e-3) / 1e9, 1)  # noqa: E731
+    return {
+        "what": "the reference's darknet_kernels.hip built for sm_100a (nvcc -O3, its build.zig flags), "
+                "launched with its own grids (gpu.zig:420-477) on GPU 0 of this box",
+        "ms_per_step": round(ms_step, 5),
+        "value": gbs((BYTES_FWD + BYTES_BWD) * E, ms_step),
+        "unit": "GB/s (this workload's algorithmic bytes, 20 B/elem, / device time)",
+        "forward_ms": round(ms_fwd, 5),
+        "backward_ms": round(ms_bwd, 5),
+        "launches_per_step": ref.launches_forward + ref.launches_backward,
+        "sgd_64Mi": {"ms": round(ms_sgd, 5), "GBps": gbs(16 * nw, ms_sgd), "launches": ref.launches_sgd},
+        "l2": f"rotating {n_sets} sets of 4 tensors ({n_sets * 4 * E * 4 / 2**20:.0f} MiB)",
+    }
+
+
 def run_reference(a):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     threads = os.cpu_count() or 1
     B, C, H, W = a.shape
+    gpu_kernels = ref_gpu_kernels(a)
     t, E = cpu_step_sample(a.shape, threads, a.steps, a.warmup)
     gbs = (BYTES_FWD + BYTES_BWD) * E / t / 1e9
     line = {
@@ -508,6 +607,8 @@ def run_reference(a):
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "elems_per_s": round(E / t, 1),
     }
+    if gpu_kernels is not None:
+        line["gpu_kernels"] = gpu_kernels
     print(json.dumps(line), flush=True)
 
 

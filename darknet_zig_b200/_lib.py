@@ -88,9 +88,14 @@ def declared_symbols() -> list[str]:
 
 
 def call(name: str, *args) -> None:
-    """Calls dnb_<name>(*args) and raises DnbError on a non-zero status."""
+    """Calls dnb_<name>(*args) and raises DnbError on a non-zero status. The argument count
+    must match the header's: ctypes would convert surplus arguments by guesswork (a pointer
+    passed as a C int is truncated) instead of refusing them."""
     L = lib()
-    st = getattr(L, "dnb_" + name)(*args)
+    fn = getattr(L, "dnb_" + name)
+    if len(args) != len(fn.argtypes):
+        raise TypeError(f"dnb_{name} takes {len(fn.argtypes)} arguments, {len(args)} given")
+    st = fn(*args)
     if st != 0:
         detail = L.dnb_last_error_detail()
         detail = detail.decode() if detail else ""

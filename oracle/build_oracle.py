@@ -7,6 +7,10 @@ Outputs:
                                by g++ for the host through hip_host_shim.h (built only
                                when the reference tree is present; it then travels with
                                the repository snapshot like any other built .so)
+  oracle/_ref/libref_gpu.so      the same kernel file compiled by nvcc for sm_100a with the
+                               reference's own flags (build.zig:144-156), behind the
+                               launchers of ref_gpu.cu: the reference's GPU path, run on the
+                               B200 as the per-op GPU baseline (same build condition)
 
 Flags: -O3 -march=x86-64-v3 (AVX2+FMA, portable across the container and the GPU box
 hosts; -march=native could emit instructions another host lacks) and -ffp-contract=off,
@@ -62,12 +66,36 @@ def build_ref_emulation(force: bool = False) -> str | None:
     return REF_EMU_SO
 
 
+REF_GPU_SO = os.path.join(REF_OUT, "libref_gpu.so")
+
+
+def build_ref_gpu(force: bool = False) -> str | None:
+    """Compile the reference's kernel file for the B200 (nvcc, sm_100a). The reference builds
+    it with `nvcc -x cu -O3 -arch=...` (build.zig:144-156), so this keeps nvcc's default
+    contraction and precision flags. Returns None when neither the reference tree nor a
+    prebuilt file is present."""
+    if not os.path.exists(REFERENCE_KERNELS):
+        return REF_GPU_SO if os.path.exists(REF_GPU_SO) else None
+    src = os.path.join(HERE, "ref_gpu.cu")
+    os.makedirs(REF_OUT, exist_ok=True)
+    if force or _stale(REF_GPU_SO, [src, REFERENCE_KERNELS, __file__]):
+        nvcc = os.path.join(os.environ.get("CUDA_HOME", "/usr/local/cuda"), "bin", "nvcc")
+        cmd = [nvcc if os.path.exists(nvcc) else "nvcc", "-x", "cu", "-O3",
+               "-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo", "-Wno-deprecated-gpu-targets",
+               "-shared", "-Xcompiler", "-fPIC", f"-DDNB_REFERENCE_KERNELS=\"{REFERENCE_KERNELS}\"",
+               "-o", REF_GPU_SO, src]
+        subprocess.check_call(cmd)
+    return REF_GPU_SO
+
+
 def build_all(force: bool = False) -> None:
     build_oracle(force)
     build_ref_emulation(force)
+    build_ref_gpu(force)
 
 
 if __name__ == "__main__":
     build_all(force="--force" in sys.argv)
     print(ORACLE_SO)
     print(REF_EMU_SO if os.path.exists(REF_EMU_SO) else "(reference emulation not built)")
+    print(REF_GPU_SO if os.path.exists(REF_GPU_SO) else "(reference GPU kernels not built)")

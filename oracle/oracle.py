@@ -3,10 +3,11 @@
 `Oracle` wraps oracle/_build/liboracle.so (the C restatement of the reference's CPU ops,
 ref_ops.c) and `RefEmulation` wraps oracle/_ref/libref_emulate.so (the reference's own
 kernel file run on the host). Both work in place on numpy float32 / int32 arrays, with
-the argument order of the reference functions they restate.
+the argument order of the reference functions they restate. `RefGpu` wraps
+oracle/_ref/libref_gpu.so, the same kernel file built for the B200 (device pointers).
 
-Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg use this module; the
-product never imports it.
+Only tests/, __graft_entry__.smoke() and bench.py's baseline legs (the CPU baseline and the
+reference arm) use this module; the product never imports it.
 """
 from __future__ import annotations
 
@@ -190,6 +191,58 @@ class RefEmulation:
 
     def __getattr__(self, name):
         return getattr(self.lib, "ref_emu_" + name)
+
+
+class RefGpu:
+    """The reference's darknet_kernels.hip built for sm_100a (oracle/_ref/libref_gpu.so),
+    launched with the reference's own grids. Arguments are device pointers (ints, e.g. a
+    torch tensor's data_ptr()) and a cudaStream_t handle; sizes are the reference's c_int.
+    Used by the GPU tests as a second parity anchor and by bench.py's reference arm as the
+    per-op GPU baseline."""
+
+    _P = C.c_void_p
+
+    def __init__(self, path: str | None = None):
+        path = path or _b.build_ref_gpu()
+        if path is None or not os.path.exists(path):
+            raise FileNotFoundError("reference GPU kernel library not built (reference tree absent)")
+        self.lib = C.CDLL(path)
+        P, I, F = self._P, C.c_int, C.c_float
+        L = self.lib
+        L.ref_gpu_conv_bn_forward.argtypes = [P] * 9 + [I, I, I, I, P]
+        L.ref_gpu_conv_bn_backward.argtypes = [P] * 11 + [I, I, I, I, P]
+        L.ref_gpu_sgd_weights.argtypes = [I, F, F, F, I, P, P, P]
+        for f in (L.ref_gpu_conv_bn_forward, L.ref_gpu_conv_bn_backward, L.ref_gpu_sgd_weights):
+            f.restype = C.c_int
+        self.launches_forward = L.ref_gpu_launches_forward()
+        self.launches_backward = L.ref_gpu_launches_backward()
+        self.launches_sgd = L.ref_gpu_launches_sgd()
+
+    def _call(self, name: str, *args) -> None:
+        # ctypes converts surplus arguments by guesswork (a pointer passed as a C int is
+        # truncated), so the count is checked against the declared argtypes first
+        fn = getattr(self.lib, "ref_gpu_" + name)
+        if len(args) != len(fn.argtypes):
+            raise TypeError(f"ref_gpu_{name} takes {len(fn.argtypes)} arguments, {len(args)} given")
+        rc = fn(*args)
+        if rc != 0:
+            raise RuntimeError(f"reference kernels ({name}): cudaError {rc}")
+
+    def conv_bn_forward(self, output, x, x_norm, mean, variance, rolling_mean, rolling_variance, scales, biases,
+                        batch, filters, spatial, act, stream=0):
+        """convolutional.zig:263-268 + batchnorm.zig:129-153 (train): `output` in place."""
+        self._call("conv_bn_forward", output, x, x_norm, mean, variance, rolling_mean, rolling_variance, scales,
+                   biases, batch, filters, spatial, act, stream)
+
+    def conv_bn_backward(self, output, delta, x, x_norm, mean, variance, scales, bias_updates, scale_updates,
+                         mean_delta, variance_delta, batch, filters, spatial, act, stream=0):
+        """convolutional.zig:279-282 + batchnorm.zig:155-170: `delta` in place."""
+        self._call("conv_bn_backward", output, delta, x, x_norm, mean, variance, scales, bias_updates,
+                   scale_updates, mean_delta, variance_delta, batch, filters, spatial, act, stream)
+
+    def sgd_weights(self, nweights, learning_rate, momentum, decay, batch, weights, weight_updates, stream=0):
+        """convolutional.zig:332-334."""
+        self._call("sgd_weights", nweights, learning_rate, momentum, decay, batch, weights, weight_updates, stream)
 
 
 _ORACLE: Oracle | None = None

@@ -56,3 +56,11 @@ def test_set_wait_limit_validates(built_lib):
     lib = _lib.lib()
     assert lib.dnb_set_wait_limit_ms(0) == 1
     assert lib.dnb_set_wait_limit_ms(2000) == 0
+
+
+def test_call_refuses_a_wrong_argument_count(built_lib):
+    # refused on the host before the library is entered
+    with pytest.raises(TypeError, match="takes 4 arguments, 5 given"):
+        _lib.call("fill", None, 4, C.c_float(0.0), None, None)
+    with pytest.raises(TypeError, match="3 given"):
+        _lib.call("fill", None, 4, C.c_float(0.0))

@@ -92,3 +92,24 @@ def test_relu_sign_of_zero_is_the_cpu_one(oracle_outputs):
     neg = d["a"] < 0
     y = oracle_outputs["activate_1"]
     assert (np.signbit(y[neg]) == False).all()  # noqa: E712
+
+
+def test_reference_gpu_bindings_match_the_launcher_signatures():
+    """oracle/_ref/libref_gpu.so (the reference's kernels built for sm_100a) is bound with
+    argtypes whose counts equal the C signatures in oracle/ref_gpu.cu, and a call with a
+    wrong count is refused on the host (no device is touched)."""
+    import re
+
+    from oracle.oracle import RefGpu
+
+    try:
+        ref = RefGpu()
+    except FileNotFoundError as e:
+        pytest.skip(str(e))
+    src = open(os.path.join(os.path.dirname(__file__), "..", "oracle", "ref_gpu.cu")).read()
+    sigs = {m.group(1): m.group(2) for m in re.finditer(r"int ref_gpu_(\w+)\(([^)]*)\)", src)}
+    for name in ("conv_bn_forward", "conv_bn_backward", "sgd_weights"):
+        n_c = len([p for p in sigs[name].split(",") if p.strip()])
+        assert len(getattr(ref.lib, "ref_gpu_" + name).argtypes) == n_c, name
+    with pytest.raises(TypeError, match="takes 8 arguments"):
+        ref._call("sgd_weights", 1, 0.1, 0.9, 5e-4, 1, 0, 0, 0, 0)
