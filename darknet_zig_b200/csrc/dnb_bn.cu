@@ -11,9 +11,9 @@
 // The obstacle is the per-channel reduction that must finish before any element can be
 // written. The persistent kernel below (the sweep) keeps the second read off HBM: channels
 // are taken in groups sized to a slice of the 126 MB L2; every CTA reduces its share of a
-// group, the CTAs exchange per-channel records through global memory, and each CTA then
-// writes the outputs of its share, re-reading the inputs from L2 (see the comment above
-// k_bn_sweep). Every wait is bounded: a CTA that gives up sets the device error word and
+// group, the CTAs exchange tagged per-channel records through global memory, and each CTA
+// then writes the outputs of its share, re-reading the inputs from L2 (see the comment
+// above kSThreads). Every wait is bounded: a CTA that gives up sets the device error word and
 // exits; the host reports DNB_ERR_TIMEOUT.
 //
 // Shapes the persistent kernel does not take (spatial % 4 != 0, unaligned pointers, more
@@ -57,9 +57,10 @@ struct BwdParam {
 };
 
 // Backward closing: s1 = sum(g), s2 = sum(g*(x-m)) over the whole (global) channel.
-__device__ __forceinline__ BwdParam bwd_close(double s1, double s2, float m, float var, float gamma, float beta,
-                                              float denom, float *bias_upd, float *scale_upd, float *mean_delta,
-                                              float *var_delta, int64_t c, bool write) {
+// bwd_params gives the apply parameters; bwd_write the per-channel outputs (the mean and
+// variance deltas are p.mdd * denom's unrounded source md and p.vd, recomputed identically).
+__device__ __forceinline__ BwdParam bwd_params(double s1, double s2, float m, float var, float gamma, float beta,
+                                               float denom, float *md_out = nullptr) {
     BwdParam p;
     p.m = m;
     p.inv = 1.0f / (sqrtf(var) + 0.000001f);
@@ -71,12 +72,22 @@ __device__ __forceinline__ BwdParam bwd_close(double s1, double s2, float m, flo
     p.vd = vd;
     p.mdd = md / denom;
     p.pad = 0.0f;
-    if (write) {
-        bias_upd[c] += (float)s1;                 // blas.zig:79
-        scale_upd[c] += (float)(s2 * (double)p.inv);  // sum(g * x_norm), blas.zig:98
-        mean_delta[c] = md;
-        var_delta[c] = vd;
-    }
+    if (md_out) *md_out = md;
+    return p;
+}
+__device__ __forceinline__ void bwd_write(double s1, double s2, const BwdParam &p, float md, float *bias_upd,
+                                          float *scale_upd, float *mean_delta, float *var_delta, int64_t c) {
+    bias_upd[c] += (float)s1;                      // blas.zig:79
+    scale_upd[c] += (float)(s2 * (double)p.inv);  // sum(g * x_norm), blas.zig:98
+    mean_delta[c] = md;
+    var_delta[c] = p.vd;
+}
+__device__ __forceinline__ BwdParam bwd_close(double s1, double s2, float m, float var, float gamma, float beta,
+                                              float denom, float *bias_upd, float *scale_upd, float *mean_delta,
+                                              float *var_delta, int64_t c, bool write) {
+    float md;
+    const BwdParam p = bwd_params(s1, s2, m, var, gamma, beta, denom, &md);
+    if (write) bwd_write(s1, s2, p, md, bias_upd, scale_upd, mean_delta, var_delta, c);
     return p;
 }
 
@@ -445,23 +456,64 @@ struct PArgs {
     const float *mean_in, *var_in;
     float *bias_upd, *scale_upd, *mean_delta, *var_delta;
     int act;
-    float4 *rec;              // [G][Ps][2 segments]
-    int cpu;                  // chunks of 32 float4s per unit
-    FastDiv f_cpu;
-    unsigned *sync;           // [0] epoch, then 2 banks of {stats_done[kMaxGroups], apply_done[kMaxGroups]}
+    unsigned long long *rec;  // this GPU's records [G][Ps][2 segments][4 words] (tagged words)
+    size_t rec_words;         // words of the whole record area (cleared when the epoch wraps)
+    int cpu, cpu_s;           // chunks per unit of the output pass / of the statistics pass
+    FastDiv f_cpu, f_cpu_s;
+    unsigned *sync;           // [0] launch epoch, [1] CTAs that have finished this launch
     unsigned *err, *abort_flag;
     unsigned long long wait_ns;
     // sync-BN across GPUs (xon, any world >= 1): every CTA stores its records of group g into
-    // every rank's buffer (xrec[r]: a peer mapping, or this GPU's own buffer for r == rank) and
-    // adds 1 to every rank's counter g (xcnt[r]); a rank has group g once its own counter
-    // passed xbase[g] + Ps * world
+    // every rank's buffer (xrec[r]: a peer mapping, or this GPU's own buffer for r == rank),
+    // tagged with the communicator's call number xtag; a rank reads them from its own buffer
     int xon, world, rank;
     int xpar;                 // call number & 1: which half of the buffers this launch uses
     int xpmax;                // CTAs a group's records have room for
-    unsigned xbase[kMaxSweepGroups];
-    float4 *xrec[kMaxRanks];
-    unsigned *xcnt[kMaxRanks];
+    unsigned xtag;
+    unsigned long long *xrec[kMaxRanks];
 };
+
+// A record is 4 64-bit words, each (tag << 32 | a float's bits): naturally aligned 64-bit
+// accesses are single-copy atomic, so a word read with this launch's tag carries this
+// launch's value, and a record whose words all carry it is complete. No fence, counter or
+// flag orders a record: the merger polls the records themselves.
+__device__ __forceinline__ unsigned long long tag_word(float v, unsigned tag) {
+    return ((unsigned long long)tag << 32) | __float_as_uint(v);
+}
+template <int NW>  // words that carry data: 3 (count, mean, M2) or 2 (two sums)
+__device__ __forceinline__ void st_record(unsigned long long *p, float4 q, unsigned tag, bool sys) {
+    const unsigned long long w0 = tag_word(q.x, tag), w1 = tag_word(q.y, tag);
+    if (sys)
+        asm volatile("st.relaxed.sys.global.v2.b64 [%0], {%1, %2};" ::"l"(p), "l"(w0), "l"(w1) : "memory");
+    else
+        asm volatile("st.relaxed.gpu.global.v2.b64 [%0], {%1, %2};" ::"l"(p), "l"(w0), "l"(w1) : "memory");
+    if constexpr (NW > 2) {
+        const unsigned long long w2 = tag_word(q.z, tag), w3 = tag_word(0.0f, tag);
+        if (sys)
+            asm volatile("st.relaxed.sys.global.v2.b64 [%0], {%1, %2};" ::"l"(p + 2), "l"(w2), "l"(w3) : "memory");
+        else
+            asm volatile("st.relaxed.gpu.global.v2.b64 [%0], {%1, %2};" ::"l"(p + 2), "l"(w2), "l"(w3) : "memory");
+    }
+}
+// true once every data word of the record at p carries `tag`; q then holds its values
+template <int NW>
+__device__ __forceinline__ bool ld_record(const unsigned long long *p, unsigned tag, bool sys, float4 &q) {
+    unsigned long long w0, w1, w2 = 0, w3 = 0;
+    if (sys)
+        asm volatile("ld.relaxed.sys.global.v2.b64 {%0, %1}, [%2];" : "=l"(w0), "=l"(w1) : "l"(p) : "memory");
+    else
+        asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];" : "=l"(w0), "=l"(w1) : "l"(p) : "memory");
+    if constexpr (NW > 2) {
+        if (sys)
+            asm volatile("ld.relaxed.sys.global.v2.b64 {%0, %1}, [%2];" : "=l"(w2), "=l"(w3) : "l"(p + 2) : "memory");
+        else
+            asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];" : "=l"(w2), "=l"(w3) : "l"(p + 2) : "memory");
+    }
+    q = make_float4(__uint_as_float((unsigned)w0), __uint_as_float((unsigned)w1), __uint_as_float((unsigned)w2), 0.0f);
+    bool ok = (unsigned)(w0 >> 32) == tag && (unsigned)(w1 >> 32) == tag;
+    if constexpr (NW > 2) ok = ok && (unsigned)(w2 >> 32) == tag;
+    return ok;
+}
 
 // Share of CTA p of a role with `parts` CTAs in group g: units [t0, t1) of the group's T,
 // in at most two channel segments (the plan keeps shares no longer than a channel).
@@ -556,16 +608,15 @@ bool persistent_disabled() {
 // running `lag` groups of statistics ahead of the outputs; each warp walks its own chunks
 // and meets the others only through shared-memory counters, so one warp's phase change
 // never drains the whole CTA. The publisher warp takes a group's per-warp partials once
-// every streaming warp has counted itself, stores the CTA's records (with a communicator:
-// into every rank's buffer over NVLink) and counts the CTA in the group's counter with a
-// release-add; the merger warp waits until every CTA (of every rank) has counted itself,
-// merges the records of the share's channels and hands the apply parameters back through
-// shared memory. A publish -- whose release waits for the record stores to land, a few
-// microseconds over NVLink -- never delays a merge, and the grid-wide exchange (several
-// L2 round trips behind saturated memory pipes) stays off the streaming path. Statistics
-// loads carry an L2 evict_last policy, output-pass loads and stores evict_first, so a group
-// stays in L2 between its two passes. Every wait is bounded; on timeout the merger sets the
-// device error word and tells the other warps to stop.
+// every streaming warp has counted itself and stores the CTA's records (with a
+// communicator: into every rank's buffer over NVLink), every word tagged with this launch's
+// tag; the merger warp polls the records of its share's channels until all carry the tag,
+// merges them and hands the apply parameters back through shared memory. No fence, counter
+// or flag sits between a record's store and its merge, so a group's exchange costs one
+// store and one poll round trip; it stays off the streaming path. Statistics loads carry
+// an L2 evict_last policy, output-pass loads and stores evict_first, so a group stays in L2
+// between its two passes. Every wait is bounded; on timeout the merger sets the device
+// error word and tells the other warps to stop.
 
 constexpr int kSThreads = 512;              // threads of a sweep CTA
 constexpr int kSMinBlocks = 2;              // CTAs per SM the register budget is set for
@@ -596,8 +647,13 @@ __device__ __forceinline__ void st4_hint(float *p, float4 v, uint64_t pol) {
 
 template <bool BWD, int A, bool HASY>
 struct SweepKernel {
-    static constexpr int UNROLL = BWD ? 2 : 4;  // float4s per tensor in flight per thread
-    static constexpr int CHUNK = 32 * UNROLL;   // float4s of one unit a warp takes at a time
+    // float4s per tensor in flight per thread: statistics loads come from HBM and get the
+    // deeper unroll; output-pass loads hit L2
+    static constexpr int UNROLL_S = BWD ? (HASY ? 2 : 2) : 4;
+    static constexpr int UNROLL = BWD ? 2 : 4;
+    static constexpr int CHUNK_S = 32 * UNROLL_S;  // float4s of one unit a statistics chunk holds
+    static constexpr int CHUNK = 32 * UNROLL;      // the same for an output-pass chunk
+    static constexpr int kRecWords = BWD ? 2 : 3;  // data words of a record
 
     // Per-group state, one buffer per group (G <= kMaxSweepGroups).
     struct Smem {
@@ -605,6 +661,7 @@ struct SweepKernel {
         float4 *wrec;    // [G][2 segments][kSWarps] per-warp partials
         float *ptab;     // [G][2 segments][8] apply parameters
         float4 *stab;    // [G][2 segments] forward parameters for the backward's stats
+        float4 *ctab;    // [G][2 segments] channel inputs: (gamma, beta) or (mean, var, gamma, beta)
         double2 *lrec;   // [G][2 segments] this rank's merged records: (mean, M2) or (sum g, sum g(x-m))
         double *lcnt;    // [G][2 segments] elements behind the forward's records
         int *done;       // [G] streaming warps that have left their partials of group g
@@ -614,7 +671,7 @@ struct SweepKernel {
     __host__ __device__ static size_t smem_bytes(int cap_units, int groups) {
         return (((size_t)groups * cap_units * sizeof(uint32_t) + 15) & ~(size_t)15) +
                (size_t)groups * (2 * kSWarps * sizeof(float4) + 2 * sizeof(double2) + 2 * sizeof(double) +
-                                 16 * sizeof(float) + 2 * sizeof(float4) + 2 * sizeof(int)) +
+                                 16 * sizeof(float) + 4 * sizeof(float4) + 2 * sizeof(int)) +
                16;
     }
     __device__ static Smem carve(const PArgs &a, unsigned char *raw) {
@@ -630,6 +687,8 @@ struct SweepKernel {
         s.lcnt = reinterpret_cast<double *>(raw + o);
         o += (size_t)G * 2 * sizeof(double);
         s.stab = reinterpret_cast<float4 *>(raw + o);
+        o += (size_t)G * 2 * sizeof(float4);
+        s.ctab = reinterpret_cast<float4 *>(raw + o);
         o += (size_t)G * 2 * sizeof(float4);
         s.ptab = reinterpret_cast<float *>(raw + o);
         o += (size_t)G * 16 * sizeof(float);
@@ -667,7 +726,6 @@ struct SweepKernel {
     }
 
     // every thread: element offsets of the units of CTA rid's share of group g into table b
-    // (and, for the backward, the forward parameters of its segments)
     __device__ static void tabulate(const PArgs &a, const Smem &s, int g, int rid, int b) {
         const Share sh = share_of(a, g, rid, a.f_ps);
         const int n_units = (int)(sh.t1 - sh.t0);
@@ -677,28 +735,43 @@ struct SweepKernel {
             a.f_k.divmod(rem, n, k);
             s.utab[b * a.cap_units + u] = (uint32_t)(((int64_t)n * a.C + sh.c0 + cl) * a.S + (int64_t)k * a.U);
         }
-        if (BWD && threadIdx.x < sh.nseg) {
-            const int64_t c = (int64_t)sh.c0 + sh.cfirst + threadIdx.x;
-            // the forward's normalisation (batchnorm.zig:142), to recompute y from x
-            s.stab[2 * b + threadIdx.x] = make_float4(a.mean_in[c], 1.0f / (sqrtf(a.var_in[c]) + 0.000001f),
-                                                      a.scales[c], a.biases[c]);
+    }
+
+    // every thread: the per-channel inputs of the (at most two) channels of each group's share,
+    // one (group, segment) per thread so that all loads are in flight at once; the merger's
+    // closing then needs no global load between a group's records and its apply parameters
+    __device__ static void load_channels(const PArgs &a, const Smem &s, int rid) {
+        for (int i = threadIdx.x; i < 2 * a.G; i += kSThreads) {
+            const int g = i >> 1, j = i & 1;
+            const Share sh = share_of(a, g, rid, a.f_ps);
+            if (j >= sh.nseg) continue;
+            const int64_t c = (int64_t)sh.c0 + sh.cfirst + j;
+            if (BWD) {
+                const float m = a.mean_in[c], v = a.var_in[c], gm = a.scales[c], bt = a.biases[c];
+                s.ctab[i] = make_float4(m, v, gm, bt);
+                // the forward's normalisation (batchnorm.zig:142), to recompute y from x
+                s.stab[i] = make_float4(m, 1.0f / (sqrtf(v) + 0.000001f), gm, bt);
+            } else {
+                s.ctab[i] = make_float4(a.scales[c], a.biases[c], 0.0f, 0.0f);
+            }
         }
     }
 
-    // The share is cut into chunks of CHUNK float4s of one unit (a unit is a.cpu chunks, the
+    // The share is cut into chunks of CH float4s of one unit (a unit is `cpu` chunks, the
     // last one possibly partial); streaming warp w takes chunks w, w + kSWarps, ... Lane l
-    // of a chunk starting at float4 k0 of its unit holds float4s k0 + l + 32 j, j < UNROLL.
+    // of a chunk starting at float4 k0 of its unit holds float4s k0 + l + 32 j, j < CH / 32.
     // A warp's chunks run through the share in order, so its segment changes at most once.
     struct Chunk {
         uint32_t off;  // element offset of the lane's first float4
         uint32_t k;    // index of that float4 within the unit
         int seg;
     };
-    __device__ static Chunk chunk_at(const PArgs &a, const Share &sh, const uint32_t *ut, uint32_t c, int lane) {
+    template <int CH>
+    __device__ static Chunk chunk_at(const Share &sh, const uint32_t *ut, const FastDiv &fcpu, uint32_t c, int lane) {
         uint32_t uo, part;
-        a.f_cpu.divmod(c, uo, part);
+        fcpu.divmod(c, uo, part);
         Chunk ch;
-        ch.k = part * CHUNK + lane;
+        ch.k = part * CH + lane;
         ch.off = ut[uo] + 4 * ch.k;
         ch.seg = sh.t0 + uo >= sh.bnd ? 1 : 0;
         return ch;
@@ -710,7 +783,7 @@ struct SweepKernel {
         const Share sh = share_of(a, g, rid, a.f_ps);
         const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
         const uint32_t u4 = (uint32_t)a.U >> 2;
-        const uint32_t n_chunks = sh.nseg ? (sh.t1 - sh.t0) * (uint32_t)a.cpu : 0;
+        const uint32_t n_chunks = sh.nseg ? (sh.t1 - sh.t0) * (uint32_t)a.cpu_s : 0;
         const uint32_t *ut = s.utab + b * a.cap_units;
         const uint64_t pol = l2_evict_last();
         float4 rec[2];
@@ -719,19 +792,19 @@ struct SweepKernel {
             Moments mo;
             float4 first = make_float4(0.0f, 0.0f, 0.0f, 0.0f);  // segment 0 once the warp moved on
             for (uint32_t c = warp; c < n_chunks; c += kSWarps) {
-                const Chunk ch = chunk_at(a, sh, ut, c, lane);
+                const Chunk ch = chunk_at<CHUNK_S>(sh, ut, a.f_cpu_s, c, lane);
                 if (ch.seg != seg) {  // warp-uniform
                     first = mo.warp_summary();
                     mo = Moments();
                     seg = ch.seg;
                 }
                 const float *p = a.t0 + ch.off;
-                float4 v[UNROLL];
+                float4 v[UNROLL_S];
 #pragma unroll
-                for (int j = 0; j < UNROLL; ++j)
+                for (int j = 0; j < UNROLL_S; ++j)
                     if (ch.k + 32 * j < u4) v[j] = ld4_hint(p + 128 * j, pol);
 #pragma unroll
-                for (int j = 0; j < UNROLL; ++j)
+                for (int j = 0; j < UNROLL_S; ++j)
                     if (ch.k + 32 * j < u4) mo.add4(v[j]);
             }
             const float4 last = mo.warp_summary();
@@ -740,7 +813,7 @@ struct SweepKernel {
         } else {
             float s1 = 0.0f, s2 = 0.0f, f1 = 0.0f, f2 = 0.0f;  // f: segment 0 once the warp moved on
             for (uint32_t c = warp; c < n_chunks; c += kSWarps) {
-                const Chunk ch = chunk_at(a, sh, ut, c, lane);
+                const Chunk ch = chunk_at<CHUNK_S>(sh, ut, a.f_cpu_s, c, lane);
                 if (ch.seg != seg) {
                     f1 = s1;
                     f2 = s2;
@@ -753,16 +826,16 @@ struct SweepKernel {
                 p.inv = fp.y;
                 p.g = fp.z;
                 p.b = fp.w;
-                float4 d[UNROLL], xv[UNROLL], yv[UNROLL];
+                float4 d[UNROLL_S], xv[UNROLL_S], yv[UNROLL_S];
 #pragma unroll
-                for (int j = 0; j < UNROLL; ++j)
+                for (int j = 0; j < UNROLL_S; ++j)
                     if (ch.k + 32 * j < u4) {
                         d[j] = ld4_hint(a.t0 + ch.off + 128 * j, pol);
                         xv[j] = ld4_hint(a.t1 + ch.off + 128 * j, pol);
                         if (HASY) yv[j] = ld4_hint(a.t2 + ch.off + 128 * j, pol);
                     }
 #pragma unroll
-                for (int j = 0; j < UNROLL; ++j)
+                for (int j = 0; j < UNROLL_S; ++j)
                     if (ch.k + 32 * j < u4) {
                         const float4 yy = HASY ? yv[j] : xv[j];
                         const float g0 = bn_grad1<A, HASY>(d[j].x, xv[j].x, yy.x, p, a.act);
@@ -790,7 +863,7 @@ struct SweepKernel {
 
     // publisher warp: one record per segment from the streaming warps' partials of group g
     // (buffer b), written to a.rec; lane 0 then publishes them and counts the CTA
-    __device__ static void publish(const PArgs &a, const Smem &s, int g, int rid, int b, unsigned *stats_done) {
+    __device__ static void publish(const PArgs &a, const Smem &s, int g, int rid, int b, unsigned tag) {
         const Share sh = share_of(a, g, rid, a.f_ps);
         const int lane = threadIdx.x & 31;
         for (int j = 0; j < sh.nseg; ++j) {
@@ -818,64 +891,36 @@ struct SweepKernel {
                 q.z = __shfl_sync(0xffffffffu, q.z, 0);
                 q.w = __shfl_sync(0xffffffffu, q.w, 0);
                 // lane r stores the record into rank r's buffer
-                if (lane < a.world)
-                    a.xrec[lane][xslot(a, g, a.rank, rid) + j] = q;
+                if (lane < a.world) st_record<kRecWords>(a.xrec[lane] + xslot(a, g, a.rank, rid, j), q, tag, true);
             } else if (lane == 0) {
-                a.rec[((int64_t)g * a.Ps + rid) * 2 + j] = q;
+                st_record<kRecWords>(a.rec + (((size_t)g * a.Ps + rid) * 2 + j) * 4, q, tag, false);
             }
-        }
-        // each storing lane's release-add publishes its records: lane 0 on this GPU, or
-        // lane r on rank r over NVLink
-        if (a.xon) {
-            if (lane < a.world)
-                asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(a.xcnt[lane] + a.xpar * kMaxSweepGroups + g)
-                             : "memory");
-        } else if (lane == 0) {
-            asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(stats_done + g) : "memory");
         }
         __syncwarp();
     }
 
-    // index of CTA p's first record of group g from rank r in an exchange buffer
-    __device__ static size_t xslot(const PArgs &a, int g, int r, int p) {
-        return ((((size_t)a.xpar * kMaxSweepGroups + g) * a.world + r) * a.xpmax + p) * 2;
-    }
-
-    // merger warp: have all CTAs of every rank published group g? (lane 0's view)
-    __device__ static bool all_published(const PArgs &a, const unsigned *stats_done, int g) {
-        if (!a.xon) return ld_acquire_gpu(stats_done + g) >= (unsigned)a.Ps;
-        unsigned v;
-        asm volatile("ld.acquire.sys.global.u32 %0, [%1];"
-                     : "=r"(v)
-                     : "l"(a.xcnt[a.rank] + a.xpar * kMaxSweepGroups + g)
-                     : "memory");
-        return (int)(v - (a.xbase[g] + (unsigned)(a.Ps * a.world))) >= 0;
+    // first word of the record (group g, segment j) of CTA p of rank r in an exchange buffer
+    __device__ static size_t xslot(const PArgs &a, int g, int r, int p, int j) {
+        return (((((size_t)a.xpar * kMaxSweepGroups + g) * a.world + r) * a.xpmax + p) * 2 + j) * 4;
     }
 
     // merger warp: merge the records of the (at most two) channels of CTA rid's share of
     // group g into s.lrec[g] -- this GPU's CTAs' records, or with a communicator every
     // rank's, in the same order on every rank (so every rank gets the same statistics).
     // Records of CTAs between the channel's first and last owner that hold no unit of it (a
-    // group with fewer units than CTAs) are skipped.
-    __device__ static void merge_local(const PArgs &a, const Smem &s, int g, int rid) {
+    // group with fewer units than CTAs) are skipped. The lanes poll their records until all
+    // carry this launch's tag (bounded; false when the wait gave up or the launch aborted).
+    __device__ static bool merge_local(const PArgs &a, const Smem &s, int g, int rid, unsigned tag) {
         const Share sh = share_of(a, g, rid, a.f_ps);
         const int lane = threadIdx.x & 31;
-        if (a.xon) {
-            // every lane acquires the counter lane 0 saw complete: orders its record loads
-            unsigned v;
-            asm volatile("ld.acquire.sys.global.u32 %0, [%1];"
-                         : "=r"(v)
-                         : "l"(a.xcnt[a.rank] + a.xpar * kMaxSweepGroups + g)
-                         : "memory");
-            (void)v;
-        }
         for (int j = 0; j < sh.nseg; ++j) {
             const int cl = sh.cfirst + j;
             const uint32_t ua = (uint32_t)cl * a.NK, ub = ua + a.NK;
             const int plo = owner_of(a, g, ua, a.Ps), phi = owner_of(a, g, ub - 1, a.Ps);
             const int per_rank = phi - plo + 1;
             const int nrec = a.xon ? per_rank * a.world : per_rank;
-            auto load = [&](int idx, float4 &dst) -> bool {
+            // 1: the record is loaded and complete; 0: no record to merge; -1: not yet written
+            auto load = [&](int idx, float4 &dst) -> int {
                 int q = 0, k = idx;
                 if (a.xon) {
                     q = idx / per_rank;
@@ -884,18 +929,46 @@ struct SweepKernel {
                 const int p = plo + k;
                 const Share o = share_of(a, g, p, a.f_ps);
                 const uint32_t lo = ua > o.t0 ? ua : o.t0, hi = ub < o.t1 ? ub : o.t1;
-                if (hi <= lo) return false;
-                dst = a.xon ? __ldcg(&a.xrec[a.rank][xslot(a, g, q, p) + (cl - o.cfirst)])
-                            : __ldcg(&a.rec[((int64_t)g * a.Ps + p) * 2 + (cl - o.cfirst)]);
-                return true;
+                if (hi <= lo) return 0;
+                const int oj = cl - o.cfirst;
+                const bool done =
+                    a.xon ? ld_record<kRecWords>(a.xrec[a.rank] + xslot(a, g, q, p, oj), tag, true, dst)
+                          : ld_record<kRecWords>(a.rec + (((size_t)g * a.Ps + p) * 2 + oj) * 4, tag, false, dst);
+                return done ? 1 : -1;
             };
             constexpr int R = 2;  // records held per lane: one L2 round trip up to 64 records
             float4 r[R];
             bool have[R];
+            {
+                const unsigned long long deadline = global_ns() + a.wait_ns;
+                unsigned polls = 0;
+                for (;;) {
+                    bool complete = true;
 #pragma unroll
-            for (int k = 0; k < R; ++k) {
-                const int idx = lane + 32 * k;
-                have[k] = idx < nrec && load(idx, r[k]);
+                    for (int k = 0; k < R; ++k) {
+                        const int idx = lane + 32 * k;
+                        const int st = idx < nrec ? load(idx, r[k]) : 0;
+                        have[k] = st == 1;
+                        complete = complete && st >= 0;
+                    }
+                    for (int idx = lane + 32 * R; idx < nrec; idx += 32) {
+                        float4 t;
+                        complete = complete && load(idx, t) >= 0;
+                    }
+                    if (__all_sync(0xffffffffu, complete)) break;
+                    int give_up = 0;
+                    if (lane == 0) {
+                        // the abort word is a second round trip: read it on every 8th poll
+                        if ((++polls & 7u) == 0 && ld_volatile(a.abort_flag)) give_up = 1;
+                        if (global_ns() > deadline) {
+                            atomicOr(a.err, a.xon ? DEVERR_WAIT_PEER : DEVERR_WAIT_BARRIER);
+                            atomicExch(a.abort_flag, 1u);
+                            give_up = 1;
+                        }
+                    }
+                    if (__shfl_sync(0xffffffffu, give_up, 0)) return false;
+                    __nanosleep(20);
+                }
             }
             double2 mine;
             if constexpr (!BWD) {
@@ -908,7 +981,7 @@ struct SweepKernel {
                     }
                 for (int idx = lane + 32 * R; idx < nrec; idx += 32) {
                     float4 t;
-                    if (!load(idx, t)) continue;
+                    if (load(idx, t) != 1) continue;
                     sn += (double)t.x;
                     smn += (double)t.x * (double)t.y;
                 }
@@ -923,7 +996,7 @@ struct SweepKernel {
                     }
                 for (int idx = lane + 32 * R; idx < nrec; idx += 32) {
                     float4 t;
-                    if (!load(idx, t)) continue;
+                    if (load(idx, t) != 1) continue;
                     const double d = (double)t.y - mu;
                     m2 += (double)t.z + (double)t.x * d * d;
                 }
@@ -940,7 +1013,7 @@ struct SweepKernel {
                     }
                 for (int idx = lane + 32 * R; idx < nrec; idx += 32) {
                     float4 t;
-                    if (!load(idx, t)) continue;
+                    if (load(idx, t) != 1) continue;
                     s1 += (double)t.x;
                     s2 += (double)t.y;
                 }
@@ -949,41 +1022,56 @@ struct SweepKernel {
             if (lane == 0) s.lrec[2 * g + j] = mine;
         }
         __syncwarp();
+        return true;
     }
 
     // merger warp: the merged statistics of the channels of CTA rid's share of group g
     // closed into the apply parameters s.ptab[g]; the CTA owning a channel's first unit
     // writes the per-channel outputs.
+    // (lane 0; from shared memory only) the apply parameters of group g into s.ptab[g]
     __device__ static void finalize(const PArgs &a, const Smem &s, int g, int rid) {
         const Share sh = share_of(a, g, rid, a.f_ps);
         const int lane = threadIdx.x & 31;
-        for (int j = 0; j < sh.nseg; ++j) {
-            const int cl = sh.cfirst + j;
-            const int64_t c = (int64_t)sh.c0 + cl;
-            const uint32_t ua = (uint32_t)cl * a.NK;
-            const bool write = owner_of(a, g, ua, a.Ps) == rid;
-            const double2 tot = s.lrec[2 * g + j];
-            const double n = s.lcnt[2 * g + j];
-            if (lane == 0) {
+        if (lane == 0)
+            for (int j = 0; j < sh.nseg; ++j) {
+                const double2 tot = s.lrec[2 * g + j];
+                const float4 ci = s.ctab[2 * g + j];
                 float *out = s.ptab + (2 * g + j) * 8;
-                const float gamma = a.scales[c], beta = a.biases[c];
                 if constexpr (!BWD) {
-                    const FwdClose f = fwd_close(tot.x, tot.y, n);
-                    if (write) {
-                        const float rm = a.rmean[c], rv = a.rvar[c];
-                        a.mean[c] = f.m;
-                        a.var[c] = f.var;
-                        a.rmean[c] = rolling(rm, f.m);
-                        a.rvar[c] = rolling(rv, f.var);
-                    }
-                    *reinterpret_cast<float4 *>(out) = make_float4(f.m, f.inv, gamma, beta);
+                    const FwdClose f = fwd_close(tot.x, tot.y, s.lcnt[2 * g + j]);
+                    *reinterpret_cast<float4 *>(out) = make_float4(f.m, f.inv, ci.x, ci.y);
                 } else {
-                    const BwdParam bp = bwd_close(tot.x, tot.y, a.mean_in[c], a.var_in[c], gamma, beta, a.denom,
-                                                  a.bias_upd, a.scale_upd, a.mean_delta, a.var_delta, c, write);
-                    *reinterpret_cast<BwdParam *>(out) = bp;
+                    *reinterpret_cast<BwdParam *>(out) = bwd_params(tot.x, tot.y, ci.x, ci.y, ci.z, ci.w, a.denom);
                 }
             }
-        }
+        __syncwarp();
+    }
+
+    // (lane 0, after the parameters are out) the per-channel outputs of group g, written by
+    // the CTA owning the channel's first unit
+    __device__ static void write_channels(const PArgs &a, const Smem &s, int g, int rid) {
+        const Share sh = share_of(a, g, rid, a.f_ps);
+        const int lane = threadIdx.x & 31;
+        if (lane == 0)
+            for (int j = 0; j < sh.nseg; ++j) {
+                const int cl = sh.cfirst + j;
+                const int64_t c = (int64_t)sh.c0 + cl;
+                if (owner_of(a, g, (uint32_t)cl * a.NK, a.Ps) != rid) continue;
+                const double2 tot = s.lrec[2 * g + j];
+                if constexpr (!BWD) {
+                    const FwdClose f = fwd_close(tot.x, tot.y, s.lcnt[2 * g + j]);
+                    const float rm = a.rmean[c], rv = a.rvar[c];
+                    a.mean[c] = f.m;
+                    a.var[c] = f.var;
+                    a.rmean[c] = rolling(rm, f.m);
+                    a.rvar[c] = rolling(rv, f.var);
+                } else {
+                    const float4 ci = s.ctab[2 * g + j];
+                    float md;
+                    const BwdParam p = bwd_params(tot.x, tot.y, ci.x, ci.y, ci.z, ci.w, a.denom, &md);
+                    bwd_write(tot.x, tot.y, p, md, a.bias_upd, a.scale_upd, a.mean_delta, a.var_delta, c);
+                }
+            }
         __syncwarp();
     }
 
@@ -999,7 +1087,7 @@ struct SweepKernel {
         const uint64_t pol = l2_evict_first();
         if constexpr (!BWD) {
             for (uint32_t c = warp; c < n_chunks; c += kSWarps) {
-                const Chunk ch = chunk_at(a, sh, ut, c, lane);
+                const Chunk ch = chunk_at<CHUNK>(sh, ut, a.f_cpu, c, lane);
                 const float4 p = *reinterpret_cast<const float4 *>(ptab + 8 * ch.seg);
                 float4 v[UNROLL];
 #pragma unroll
@@ -1024,7 +1112,7 @@ struct SweepKernel {
             }
         } else {
             for (uint32_t c = warp; c < n_chunks; c += kSWarps) {
-                const Chunk ch = chunk_at(a, sh, ut, c, lane);
+                const Chunk ch = chunk_at<CHUNK>(sh, ut, a.f_cpu, c, lane);
                 const BwdParam p = *reinterpret_cast<const BwdParam *>(ptab + 8 * ch.seg);
                 float4 d[UNROLL], xv[UNROLL], yv[UNROLL];
 #pragma unroll
@@ -1050,79 +1138,42 @@ struct SweepKernel {
     }
 };
 
+// The roles of a sweep CTA; each returns when its work is done or a wait gave up.
 template <bool BWD, int A, bool HASY>
-__global__ void __launch_bounds__(kSThreads, kSMinBlocks) k_bn_sweep(PArgs a) {
+__device__ void sweep_publisher(const PArgs &a, const typename SweepKernel<BWD, A, HASY>::Smem &s, int rid,
+                                unsigned tag) {
     using K = SweepKernel<BWD, A, HASY>;
-    extern __shared__ __align__(128) unsigned char smem_raw[];
-    const typename K::Smem s = K::carve(a, smem_raw);
-    __shared__ unsigned s_epoch;
-    const int rid = (int)blockIdx.x;
-    if (threadIdx.x == 0) {
-        s_epoch = ld_volatile(&a.sync[0]);
-        *s.stop = 0;
+    // groups in order, as soon as every streaming warp's partials are in
+    for (int g = 0; g < a.G; ++g) {
+        if (!K::wait_smem(a, s, &s.done[g], kSWarps)) return;
+        K::publish(a, s, g, rid, g, tag);
     }
-    if (threadIdx.x < a.G) {
-        s.done[threadIdx.x] = 0;
-        s.ready[threadIdx.x] = 0;
-    }
-    for (int g = 0; g < a.G; ++g) K::tabulate(a, s, g, rid, g);
-    __syncthreads();
-    const unsigned epoch = s_epoch;
-    unsigned *stats_done = a.sync + 1 + (size_t)(epoch & 1u) * 2 * kMaxGroups;
-    const int warp = threadIdx.x >> 5;
+}
+template <bool BWD, int A, bool HASY>
+__device__ void sweep_merger(const PArgs &a, const typename SweepKernel<BWD, A, HASY>::Smem &s, int rid,
+                             unsigned tag) {
+    using K = SweepKernel<BWD, A, HASY>;
     const int lane = threadIdx.x & 31;
-    if (warp == kSWarps) {
-        // publisher: groups in order, as soon as every streaming warp's partials are in
-        if (rid == 0) {  // the next launch's bank
-            unsigned *other = a.sync + 1 + (size_t)((epoch & 1u) ^ 1u) * 2 * kMaxGroups;
-            for (int i = lane; i < 2 * kMaxGroups; i += 32) other[i] = 0u;
+    // groups in order, once the records of the share's channels (of every rank) are in
+    for (int g = 0; g < a.G; ++g) {
+        if (!K::merge_local(a, s, g, rid, tag)) {
+            if (lane == 0) *reinterpret_cast<volatile int *>(s.stop) = 1;
+            return;
         }
-        for (int g = 0; g < a.G; ++g) {
-            if (!K::wait_smem(a, s, &s.done[g], kSWarps)) return;
-            K::publish(a, s, g, rid, g, stats_done);
+        K::finalize(a, s, g, rid);
+        if (lane == 0) {
+            __threadfence_block();
+            *reinterpret_cast<volatile int *>(&s.ready[g]) = 1;
         }
-        return;
+        __syncwarp();
+        K::write_channels(a, s, g, rid);
     }
-    if (warp == kSWarps + 1) {
-        // merger: groups in order, once every CTA (of every rank) has published
-        for (int g = 0; g < a.G; ++g) {
-            int ok = 1;
-            if (lane == 0) {
-                const unsigned long long deadline = global_ns() + a.wait_ns;
-                while (!K::all_published(a, stats_done, g)) {
-                    if (ld_volatile(a.abort_flag)) {
-                        ok = 0;
-                        break;
-                    }
-                    if (global_ns() > deadline) {
-                        atomicOr(a.err, a.xon ? DEVERR_WAIT_PEER : DEVERR_WAIT_BARRIER);
-                        atomicExch(a.abort_flag, 1u);
-                        ok = 0;
-                        break;
-                    }
-                    __nanosleep(32);
-                }
-            }
-            ok = __shfl_sync(0xffffffffu, ok, 0);
-            __syncwarp();  // lane 0's acquire orders the other lanes' record loads
-            if (!ok) {
-                if (lane == 0) *reinterpret_cast<volatile int *>(s.stop) = 1;
-                return;
-            }
-            // every CTA has read the epoch once all have counted themselves in group 0
-            if (g == 0 && rid == 0 && lane == 0) atomicExch(&a.sync[0], epoch + 1);
-            K::merge_local(a, s, g, rid);
-            K::finalize(a, s, g, rid);
-            if (lane == 0) {
-                __threadfence_block();
-                *reinterpret_cast<volatile int *>(&s.ready[g]) = 1;
-            }
-            __syncwarp();
-        }
-        return;
-    }
-    // streaming warps: statistics of groups 0 .. lag-1, then per group g the statistics of
-    // group g + lag followed by the outputs of group g
+}
+template <bool BWD, int A, bool HASY>
+__device__ void sweep_streamer(const PArgs &a, const typename SweepKernel<BWD, A, HASY>::Smem &s, int rid) {
+    using K = SweepKernel<BWD, A, HASY>;
+    // statistics of groups 0 .. lag-1, then per group g the statistics of group g + lag
+    // followed by the outputs of group g
     for (int h = 0; h < a.depth && h < a.G; ++h) K::stats(a, s, h, rid, h);
     for (int g = 0; g < a.G; ++g) {
         if (g + a.depth < a.G) K::stats(a, s, g + a.depth, rid, g + a.depth);
@@ -1131,12 +1182,73 @@ __global__ void __launch_bounds__(kSThreads, kSMinBlocks) k_bn_sweep(PArgs a) {
     }
 }
 
+template <bool BWD, int A, bool HASY>
+__global__ void __launch_bounds__(kSThreads, kSMinBlocks) k_bn_sweep(PArgs a) {
+    using K = SweepKernel<BWD, A, HASY>;
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    const typename K::Smem s = K::carve(a, smem_raw);
+    __shared__ unsigned s_epoch;
+    __shared__ int s_exited;
+    const int rid = (int)blockIdx.x;
+    if (threadIdx.x == 0) {
+        s_epoch = ld_volatile(&a.sync[0]);
+        *s.stop = 0;
+        s_exited = 0;
+    }
+    if (threadIdx.x < a.G) {
+        s.done[threadIdx.x] = 0;
+        s.ready[threadIdx.x] = 0;
+    }
+    for (int g = 0; g < a.G; ++g) K::tabulate(a, s, g, rid, g);
+    K::load_channels(a, s, rid);
+    __syncthreads();
+    // this launch's record tag: the communicator's call number, or the launch epoch + 1
+    // (never 0, the tag of a cleared record)
+    const unsigned epoch = s_epoch;
+    const unsigned tag = a.xon ? a.xtag : epoch + 1u;
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    // The epoch advances once per launch, after every CTA has read it; the next launch on
+    // this stream starts after this one has ended. In the launch whose successor's tag would
+    // wrap to 0 the record area is cleared first, once no CTA reads records any more: there
+    // the last warp of the last CTA to finish does it (once per 2^32 - 1 launches). In every
+    // other launch the last CTA whose publisher is done does it, off the kernel's tail.
+    const bool wraps = epoch + 2u == 0u;
+    if (warp == kSWarps) {
+        sweep_publisher<BWD, A, HASY>(a, s, rid, tag);
+        __syncwarp();
+        if (!wraps && lane == 0 && atomicAdd(&a.sync[1], 1u) == (unsigned)a.Ps - 1u) {
+            a.sync[1] = 0u;
+            a.sync[0] = epoch + 1u;
+        }
+    } else if (warp == kSWarps + 1) {
+        sweep_merger<BWD, A, HASY>(a, s, rid, tag);
+    } else {
+        sweep_streamer<BWD, A, HASY>(a, s, rid);
+    }
+    if (!wraps) return;
+    __syncwarp();
+    int last = 0;
+    if (lane == 0 && atomicAdd(&s_exited, 1) == kSThreads / 32 - 1)
+        last = atomicAdd(&a.sync[1], 1u) == (unsigned)a.Ps - 1u;
+    if (!__shfl_sync(0xffffffffu, last, 0)) return;
+    for (size_t i = lane; i < a.rec_words; i += 32) a.rec[i] = 0ull;
+    __syncwarp();
+    if (lane == 0) {
+        a.sync[1] = 0u;
+        a.sync[0] = 0u;
+    }
+}
+
 // Sweep plan: P = CTAs per SM x SMs; channel groups whose inputs fill about
-// DNB_BN_GROUP_MB (default 32 MiB), at most kMaxSweepGroups of them; lag = groups whose
-// statistics run ahead of the outputs, as many as keep lag + 1 groups within DNB_BN_L2_MB
-// (default 64 MiB) of L2, so that the grid exchange of a group is hidden behind later
+// DNB_BN_GROUP_MB per input tensor (default 32 MiB forward, 16 MiB backward), at most
+// kMaxSweepGroups of them; lag = groups whose statistics run ahead of the outputs, as many
+// as keep lag + 1 groups within DNB_BN_L2_MB per input tensor (default 64 MiB forward,
+// 32 MiB backward) of L2, so that the grid exchange of a group is hidden behind later
 // statistics passes (or, when the whole input fits, every statistics pass runs before the
-// first output pass); units of U = spatial/K floats with K the smallest divisor giving
+// first output pass). The defaults are the fastest measured at BASELINE configs 0/1 on the
+// B200: the forward's single input fits L2 in two groups; the backward's two inputs do not,
+// and smaller groups with a lag of one keep its output pass in L2; units of U = spatial/K floats with K the smallest divisor giving
 // >= 8 units per CTA in a group (U >= 256 floats); cg <= P keeps a share within two
 // channels.
 template <bool BWD, bool HASY>
@@ -1149,7 +1261,7 @@ PPlan plan_sweep(int64_t batch, int64_t filters, int64_t spatial, const DeviceSt
     if (ctas > 2048 / kSThreads) ctas = 2048 / kSThreads;
     const int64_t P = (int64_t)ds->sm_count * ctas;
     const int64_t bytes_per_channel = batch * spatial * 4 * nt;
-    const int64_t budget = ((int64_t)env_int("DNB_BN_GROUP_MB", 32, 1, 4096) << 20) * nt;
+    const int64_t budget = ((int64_t)env_int("DNB_BN_GROUP_MB", BWD ? 16 : 32, 1, 4096) << 20) * nt;
     int64_t cg = budget / bytes_per_channel;
     if (cg < 1) cg = 1;
     if (cg > P) cg = P;
@@ -1176,7 +1288,7 @@ PPlan plan_sweep(int64_t batch, int64_t filters, int64_t spatial, const DeviceSt
     pl.cg = (int)cg;
     pl.G = (int)G;
     pl.P = (int)P;
-    const int64_t l2 = ((int64_t)env_int("DNB_BN_L2_MB", 64, 1, 4096) << 20) * nt;
+    const int64_t l2 = ((int64_t)env_int("DNB_BN_L2_MB", BWD ? 32 : 64, 1, 4096) << 20) * nt;
     int64_t lag = l2 / (cg * bytes_per_channel) - 1;
     if (lag > G - 1) lag = G - 1;
     if (lag < 0) lag = 0;
@@ -1238,13 +1350,17 @@ dnb_status run_sweep(int64_t batch, int64_t filters, int64_t spatial, int act, P
             smem_set = pl.smem;
         }
         Workspace *ws = nullptr;
-        DNB_TRY(workspace(stream, sizeof(float4) * (size_t)pl.G * pl.P * 2, &ws));
+        DNB_TRY(workspace(stream, 0, &ws, (size_t)pl.G * pl.P * 2 * 4));
         fill_partition(a, pl, batch, filters, spatial);
         constexpr int chunk = SweepKernel<BWD, A, HASY>::CHUNK;
+        constexpr int chunk_s = SweepKernel<BWD, A, HASY>::CHUNK_S;
         a.cpu = (pl.U / 4 + chunk - 1) / chunk;
         a.f_cpu = FastDiv((uint32_t)a.cpu);
+        a.cpu_s = (pl.U / 4 + chunk_s - 1) / chunk_s;
+        a.f_cpu_s = FastDiv((uint32_t)a.cpu_s);
         a.act = act;
-        a.rec = static_cast<float4 *>(ws->scratch);
+        a.rec = ws->recs;
+        a.rec_words = ws->rec_words;
         a.sync = ws->sync;
         a.err = ds->error_word;
         a.abort_flag = ds->abort_flag;
@@ -1259,11 +1375,8 @@ dnb_status run_sweep(int64_t batch, int64_t filters, int64_t spatial, int act, P
             a.rank = cv->rank;
             a.xpar = (int)(cv->tag & 1u);
             a.xpmax = cv->pmax;
-            for (int g = 0; g < kMaxSweepGroups; ++g) a.xbase[g] = cv->base[g];
-            for (int r = 0; r < cv->world; ++r) {
-                a.xrec[r] = cv->rec[r];
-                a.xcnt[r] = cv->cnt[r];
-            }
+            a.xtag = cv->tag;
+            for (int r = 0; r < cv->world; ++r) a.xrec[r] = cv->rec[r];
             // normalize_delta divides by the element count of the whole batch
             a.denom = (float)(batch * spatial * cv->world);
             int e2 = 0;
@@ -1282,8 +1395,6 @@ dnb_status run_sweep(int64_t batch, int64_t filters, int64_t spatial, int act, P
         cfg.numAttrs = 1;
         DNB_CUDA(cudaLaunchKernelEx(&cfg, kern, a));
         *launched = true;
-        if (cv)  // every CTA of every rank adds 1 to each counter of the groups this launch uses
-            for (int g = 0; g < pl.G; ++g) cv->base[g] += (unsigned)(pl.P * cv->world);
         return after_launch(stream, what);
     });
 }

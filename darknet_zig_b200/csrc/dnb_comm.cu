@@ -1,17 +1,15 @@
 // Sync-BN communicator: each rank's exchange buffer, shared with the other ranks through
 // CUDA IPC so that the fused sweep kernel can store its CTAs' per-channel records straight
-// into every peer's memory over NVLink and count them there with remote atomics. No
-// collective library is on this path; the host only swaps the 64-byte IPC handles once
-// (any transport).
+// into every peer's memory over NVLink. No collective library is on this path; the host only
+// swaps the 64-byte IPC handles once (any transport).
 //
-// Buffer of one rank: records float4 [2 parities][kMaxSweepGroups][world][pmax][2], then
-// arrival counters u32 [2 parities][kMaxSweepGroups]. A launch with call number t uses
-// parity t & 1; its CTAs store their records of group g into every rank's buffer and add 1
-// to every rank's counter g of that parity, so a rank has all of group g once its counter
-// passed base + P * world. Counters only grow: the host keeps each counter's expected value
-// (base), identical on every rank because every rank makes the same calls with the same
-// shapes. A rank can start call t+1 while a slower peer still reads the records of call t,
-// never call t+2 (that needs the slower peer's records of call t+1).
+// Buffer of one rank: tagged records, 64-bit words
+// [2 parities][kMaxSweepGroups][world][pmax][2 segments][4]. A launch with call number t
+// (never 0; identical on every rank because every rank makes the same calls) uses parity
+// t & 1 and tags every word it stores with t; a rank has a record once all its words carry
+// t. A rank can start call t+1 while a slower peer still reads the records of call t, never
+// call t+2 (that needs the slower peer's records of call t+1). Tags repeat after 2^32 - 1
+// calls of one communicator.
 #include <string.h>
 
 #include "dnb_common.cuh"
@@ -22,7 +20,6 @@ struct Comm {
     int rank = 0, world = 1, device = 0, pmax = 0;
     int64_t cmax = 0;
     size_t rec_bytes = 0, bytes = 0;
-    unsigned base[2][kMaxSweepGroups] = {};
     void *local = nullptr;
     void *peer[kMaxRanks] = {};  // opened IPC mappings (peer[rank] = local)
     bool connected = false;
@@ -44,11 +41,7 @@ dnb_status comm_next(dnb_comm handle, CommView *out) {
     out->tag = c->calls;
     out->cmax = c->cmax;
     out->pmax = c->pmax;
-    for (int r = 0; r < c->world; ++r) {
-        out->rec[r] = static_cast<float4 *>(c->peer[r]);
-        out->cnt[r] = reinterpret_cast<unsigned *>(static_cast<char *>(c->peer[r]) + c->rec_bytes);
-    }
-    out->base = c->base[c->calls & 1u];
+    for (int r = 0; r < c->world; ++r) out->rec[r] = static_cast<unsigned long long *>(c->peer[r]);
     return DNB_OK;
 }
 
@@ -73,8 +66,8 @@ dnb_status dnb_comm_init(int rank, int world, int64_t max_channels, void *handle
     c->device = ds->device;
     c->cmax = max_channels;
     c->pmax = ds->sm_count * 4;  // the sweep runs at most 4 CTAs per SM
-    c->rec_bytes = sizeof(float4) * 2 * (size_t)kMaxSweepGroups * world * c->pmax * 2;
-    c->bytes = c->rec_bytes + sizeof(unsigned) * 2 * kMaxSweepGroups;
+    c->rec_bytes = sizeof(unsigned long long) * 2 * (size_t)kMaxSweepGroups * world * c->pmax * 2 * 4;
+    c->bytes = c->rec_bytes;
     cudaError_t e = cudaMalloc(&c->local, c->bytes);
     if (e == cudaSuccess) e = cudaMemset(c->local, 0, c->bytes);
     cudaIpcMemHandle_t h;

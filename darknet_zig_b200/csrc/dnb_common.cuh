@@ -53,39 +53,38 @@ struct DeviceState {
 // Scratch owned by the library for one (device, stream) pair.
 struct Workspace {
     cudaStream_t stream = nullptr;
-    // grid-barrier state: [0] = launch epoch, [1..] two banks of per-group arrival counters
+    // persistent-kernel state: [0] = launch epoch, [1] = CTAs that finished the current launch
     unsigned *sync = nullptr;
     size_t sync_words = 0;
-    void *scratch = nullptr;  // per-channel partial records
+    void *scratch = nullptr;  // per-channel partials of the multi-launch paths
     size_t scratch_bytes = 0;
+    // the sweep's tagged per-CTA records (64-bit words), cleared when allocated or reset
+    unsigned long long *recs = nullptr;
+    size_t rec_words = 0;
 };
 
-// `sync` = 1 epoch word + 2 banks, each holding two arrays of kMaxGroups group counters.
-constexpr int kMaxGroups = 1024;
-constexpr size_t kSyncWords = 1 + 4 * (size_t)kMaxGroups;
+constexpr size_t kSyncWords = 2;
 
 // A sync-BN communicator as a kernel sees it (dnb_comm.cu): this rank, the ranks, and every
-// rank's exchange buffer: records float4 [2 parities][kMaxSweepGroups][world][pmax CTAs][2]
-// and arrival counters u32 [2 parities][kMaxSweepGroups]. Counters only grow; base[g] is
-// what counter g of this launch's parity held before the launch (the host keeps it).
+// rank's exchange buffer of tagged records, 64-bit words
+// [2 parities][kMaxSweepGroups][world][pmax CTAs][2 segments][4].
 constexpr int kMaxRanks = 8;
 constexpr int kMaxSweepGroups = 16;
 struct CommView {
     int rank = 0, world = 1;
-    unsigned tag = 0;  // the call number; parity = tag & 1
+    unsigned tag = 0;  // the call number (never 0): the records' tag; parity = tag & 1
     int pmax = 0;      // CTAs a group's records have room for
     int64_t cmax = 0;
-    float4 *rec[kMaxRanks] = {};
-    unsigned *cnt[kMaxRanks] = {};
-    unsigned *base = nullptr;  // host: [kMaxSweepGroups] counters' values before this launch
+    unsigned long long *rec[kMaxRanks] = {};
 };
 // The view of `comm` for its next fused call on the current device (advances its call number).
 dnb_status comm_next(dnb_comm comm, CommView *out);
 
 // The state of the current device, initialising it on first use.
 dnb_status current_device(DeviceState **out);
-// The workspace of (current device, stream) with at least `scratch_bytes` of scratch.
-dnb_status workspace(cudaStream_t stream, size_t scratch_bytes, Workspace **out);
+// The workspace of (current device, stream) with at least `scratch_bytes` of scratch and
+// `rec_words` record words.
+dnb_status workspace(cudaStream_t stream, size_t scratch_bytes, Workspace **out, size_t rec_words = 0);
 // Checks the launch that was just issued (and synchronises under sync-after-launch).
 dnb_status after_launch(cudaStream_t stream, const char *what);
 // Counts one device-side launch (kernel or memset) for dnb_launch_count; after_launch does it.

@@ -68,7 +68,7 @@ dnb_status current_device(DeviceState **out) {
     return DNB_OK;
 }
 
-dnb_status workspace(cudaStream_t stream, size_t scratch_bytes, Workspace **out) {
+dnb_status workspace(cudaStream_t stream, size_t scratch_bytes, Workspace **out, size_t rec_words) {
     int device = 0;
     DNB_CUDA(cudaGetDevice(&device));
     std::lock_guard<std::mutex> lock(g_mu);
@@ -79,7 +79,8 @@ dnb_status workspace(cudaStream_t stream, size_t scratch_bytes, Workspace **out)
     const size_t want_sync = kSyncWords;
     bool grow_sync = ws->sync_words < want_sync;
     bool grow_scratch = ws->scratch_bytes < scratch_bytes;
-    if (grow_sync || grow_scratch) {
+    bool grow_recs = ws->rec_words < rec_words;
+    if (grow_sync || grow_scratch || grow_recs) {
         cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
         DNB_CUDA(cudaStreamIsCapturing(stream, &cap));
         if (cap != cudaStreamCaptureStatusNone)
@@ -101,6 +102,16 @@ dnb_status workspace(cudaStream_t stream, size_t scratch_bytes, Workspace **out)
         ws->scratch = nullptr;
         DNB_CUDA(cudaMalloc(&ws->scratch, bytes));
         ws->scratch_bytes = bytes;
+    }
+    if (grow_recs) {
+        // a record word is (tag << 32 | value) and tag 0 is never a launch's: cleared words
+        // read as "not written"
+        size_t words = rec_words < (1u << 16) ? (1u << 16) : rec_words;
+        if (ws->recs) DNB_CUDA(cudaFree(ws->recs));
+        ws->recs = nullptr;
+        DNB_CUDA(cudaMalloc(&ws->recs, words * sizeof(unsigned long long)));
+        DNB_CUDA(cudaMemset(ws->recs, 0, words * sizeof(unsigned long long)));
+        ws->rec_words = words;
     }
     *out = ws;
     return DNB_OK;
@@ -232,14 +243,18 @@ dnb_status dnb_check_device_error(void) {
     unsigned word[2] = {0, 0};
     DNB_CUDA(cudaMemcpy(word, ds->error_word, sizeof(word), cudaMemcpyDeviceToHost));
     if (word[0] == 0 && word[1] == 0) return DNB_OK;
-    // A wait gave up: the barrier counters of every workspace on this device may be
-    // mid-launch, so they are reset along with the error word.
+    // A wait gave up: the launch state of every workspace on this device may be mid-launch,
+    // so it is reset along with the error word (the epoch restarts, so the records carrying
+    // earlier epochs' tags are cleared too).
     DNB_CUDA(cudaMemset(ds->error_word, 0, 2 * sizeof(unsigned)));
     {
         std::lock_guard<std::mutex> lock(g_mu);
-        for (auto &kv : g_ws)
-            if (kv.first.first == ds->device && kv.second->sync)
-                DNB_CUDA(cudaMemset(kv.second->sync, 0, kv.second->sync_words * sizeof(unsigned)));
+        for (auto &kv : g_ws) {
+            if (kv.first.first != ds->device) continue;
+            if (kv.second->sync) DNB_CUDA(cudaMemset(kv.second->sync, 0, kv.second->sync_words * sizeof(unsigned)));
+            if (kv.second->recs)
+                DNB_CUDA(cudaMemset(kv.second->recs, 0, kv.second->rec_words * sizeof(unsigned long long)));
+        }
     }
     return fail(DNB_ERR_TIMEOUT, "a device-side wait gave up (error bits 0x%x)", word[0]);
 }
