@@ -470,6 +470,18 @@ def cpu_step_sample(shape, threads, steps, warmup):
     return sum(times) / len(times), E
 
 
+def cpu_model() -> str:
+    """The host CPU's model name (/proc/cpuinfo), for the baseline lines."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown CPU"
+
+
 def cpu_baseline(a, threads):
     # a bounded sample: as many full steps as fit ~10 s at this core count (at least 2)
     t_one, E = cpu_step_sample(a.shape, threads, 1, 0)
@@ -478,7 +490,8 @@ def cpu_baseline(a, threads):
     gbs = (BYTES_FWD + BYTES_BWD) * E / t / 1e9
     return {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
             "sample": f"{steps} full steps of the workload (BN+leaky fwd+bwd, {E} elements) through the C "
-                      f"restatement of the reference CPU ops; {t * 1e3:.1f} ms/step; host {os.cpu_count()} cpus",
+                      f"restatement of the reference CPU ops; {t * 1e3:.1f} ms/step; host {os.cpu_count()} cpus "
+                      f"({cpu_model()})",
             "ms_per_step": round(t * 1e3, 2), "elems_per_s": round(E / t, 1)}
 
 
@@ -603,7 +616,8 @@ def run_reference(a):
                    "parallelism": "host cores (reference CPU ops, OpenMP over channels)"},
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
                          "sample": f"{a.steps} full steps (after {a.warmup} warm-up) of the reference op sequence "
-                                   f"batchnorm.zig:74-123 + activations.zig, C restatement in oracle/"},
+                                   f"batchnorm.zig:74-123 + activations.zig, C restatement in oracle/; "
+                                   f"{threads} threads of {cpu_model()}"},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "elems_per_s": round(E / t, 1),
     }

@@ -346,3 +346,31 @@ def test_syncbn_split_path_two_shards_on_one_gpu(cuda):
             assert_close(host(got), host(want), f"sync {name}", rtol=1e-5, atol=1e-5)
         half = slice(i * h * C * S, (i + 1) * h * C * S)
         assert_close(host(dx), host(dx_full)[half], "sync dx", rtol=1e-4, atol=1e-5)
+
+
+def test_rolling_statistics_survive_a_weights_round_trip(cuda, tmp_path):
+    """Rolling statistics produced by the fused training forward, saved in the reference's
+    .weights layout (parser.zig:535-543) and loaded into a fresh layer, give a bit-identical
+    inference forward."""
+    from darknet_zig_b200 import weights
+
+    B, C, H, W = 8, 16, 8, 8
+    bn = BatchNorm(B, C, H, W)
+    bn.scales.copy_(dev(synth.uniform(40, (C,), 0.5, 1.5)))
+    bn.biases.copy_(dev(synth.normal(41, (C,), 0.0, 0.1)))
+    for k in range(3):
+        bn.forward(dev(synth.normal(42 + k, (B * C * H * W,), 0.3, 1.2)), train=True)
+    x_test = dev(synth.normal(50, (B * C * H * W,), 0.0, 1.0))
+    y_before = host(bn.forward(x_test, train=False))
+    assert host(bn.rolling_variance).any()
+    path = str(tmp_path / "bn.weights")
+    p = weights.batchnorm_params(bn, kind="convolutional", nweights=C * 4 * 9)
+    p.pull()
+    weights.save(path, [p], seen=24)
+    fresh = BatchNorm(B, C, H, W)
+    q = weights.batchnorm_params(fresh, kind="convolutional", nweights=C * 4 * 9)
+    assert weights.load(path, [q]) == 24
+    q.push()
+    for name in ("scales", "biases", "rolling_mean", "rolling_variance"):
+        assert_bitexact(host(getattr(fresh, name)), host(getattr(bn, name)), name)
+    assert_bitexact(host(fresh.forward(x_test, train=False)), y_before, "inference output")

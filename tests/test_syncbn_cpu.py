@@ -7,7 +7,8 @@ reduce_backward_partials), and merges. The merged statistics must be identical o
 ranks and agree with the reference's mean / unbiased variance (blas.zig:106-135) of the
 whole batch. Failures are made on the host: a rank that raises before the exchange, and a
 rank that stays alive but never joins it; the surviving rank must get an error from the
-process group within its timeout instead of waiting for good."""
+process group within its timeout instead of waiting for good. A rank that joins late but
+within the timeout delays the exchange without changing its result."""
 from __future__ import annotations
 
 import json
@@ -58,6 +59,8 @@ def _worker(rank: int, port: int, mode: str, outdir: str) -> None:
         gathered = torch.empty(WORLD, C, 2, dtype=torch.float64)
         if mode == "raise" and rank == 1:
             raise RuntimeError("injected failure before the exchange")
+        if mode == "delay" and rank == 1:
+            time.sleep(PG_TIMEOUT_S / 2)  # late, but within the process group's timeout
         if mode == "absent" and rank == 1:
             time.sleep(PG_TIMEOUT_S + 4)  # alive, but never joins the exchange
             res["absent"] = True
@@ -139,3 +142,15 @@ def test_a_rank_that_never_joins_times_out_the_exchange(tmp_path):
     assert res[1].get("absent")
     assert "error" in res[0], "the exchange completed without one rank"
     assert res[0]["seconds"] < PG_TIMEOUT_S + 30
+
+
+def test_a_late_rank_delays_the_exchange_without_changing_it(tmp_path):
+    (tmp_path / "ok").mkdir()
+    (tmp_path / "late").mkdir()
+    ok = _run("ok", tmp_path / "ok")
+    late = _run("delay", tmp_path / "late")
+    for r in late:
+        assert "error" not in r, r
+    assert late[0]["seconds"] >= PG_TIMEOUT_S / 2 - 0.5  # rank 0 waited for its peer
+    for key in ("mean", "var", "bsum"):
+        assert late[0][key] == ok[0][key] == late[1][key]
