@@ -737,11 +737,12 @@ struct SweepKernel {
         }
     }
 
-    // every thread: the per-channel inputs of the (at most two) channels of each group's share,
-    // one (group, segment) per thread so that all loads are in flight at once; the merger's
-    // closing then needs no global load between a group's records and its apply parameters
-    __device__ static void load_channels(const PArgs &a, const Smem &s, int rid) {
-        for (int i = threadIdx.x; i < 2 * a.G; i += kSThreads) {
+    // threads t0, t0 + nt, ...: the per-channel inputs of the (at most two) channels of each
+    // group's share, one (group, segment) per thread so that all loads are in flight at once;
+    // the merger's closing then needs no global load between a group's records and its apply
+    // parameters
+    __device__ static void load_channels(const PArgs &a, const Smem &s, int rid, int t0, int nt) {
+        for (int i = t0; i < 2 * a.G; i += nt) {
             const int g = i >> 1, j = i & 1;
             const Share sh = share_of(a, g, rid, a.f_ps);
             if (j >= sh.nseg) continue;
@@ -1154,6 +1155,10 @@ __device__ void sweep_merger(const PArgs &a, const typename SweepKernel<BWD, A, 
                              unsigned tag) {
     using K = SweepKernel<BWD, A, HASY>;
     const int lane = threadIdx.x & 31;
+    if (!BWD) {
+        K::load_channels(a, s, rid, lane, 32);
+        __syncwarp();
+    }
     // groups in order, once the records of the share's channels (of every rank) are in
     for (int g = 0; g < a.G; ++g) {
         if (!K::merge_local(a, s, g, rid, tag)) {
@@ -1200,7 +1205,9 @@ __global__ void __launch_bounds__(kSThreads, kSMinBlocks) k_bn_sweep(PArgs a) {
         s.ready[threadIdx.x] = 0;
     }
     for (int g = 0; g < a.G; ++g) K::tabulate(a, s, g, rid, g);
-    K::load_channels(a, s, rid);
+    // the backward's statistics pass needs the forward's parameters at once; the forward's
+    // channel inputs are only the merger's, which loads them itself off the prologue
+    if (BWD) K::load_channels(a, s, rid, threadIdx.x, kSThreads);
     __syncthreads();
     // this launch's record tag: the communicator's call number, or the launch epoch + 1
     // (never 0, the tag of a cleared record)
