@@ -23,7 +23,8 @@ from parity import assert_bitexact, assert_close, channel_view, exact_channel_su
 pytestmark = pytest.mark.gpu
 
 # (batch, filters, spatial): generic path (S % 4 != 0), persistent path at several unit
-# shapes, the gputest shape, and the BASELINE configs 0/1 and 4 (per GPU)
+# shapes, the gputest shape, and the BASELINE configs 0/1 and 4 (per GPU) plus a 32 MiB
+# single-group forward
 SHAPES = [
     (4, 17, 53),
     (8, 16, 64),
@@ -33,7 +34,7 @@ SHAPES = [
     (64, 64, 3136),
     (1, 300, 100),
 ]
-FULL_SHAPES = [(128, 128, 1024), (128, 256, 784)]
+FULL_SHAPES = [(128, 128, 1024), (128, 256, 784), (64, 128, 1024)]
 
 
 def dev(a):
@@ -175,7 +176,8 @@ def test_fused_backward(cuda, oracle, shape, act, with_y):
 @pytest.mark.slow
 @pytest.mark.parametrize("shape", FULL_SHAPES)
 def test_fused_full_size_forward_backward(cuda, oracle, shape):
-    """BASELINE configs 0/1 (128x128x32x32) and 4 (per GPU 128x256x28x28), leaky 0.1."""
+    """BASELINE configs 0/1 (128x128x32x32) and 4 (per GPU 128x256x28x28), leaky 0.1, and a
+    32 MiB tensor whose forward plan is a single channel group."""
     test_fused_forward_train(cuda, oracle, shape, gpu.LEAKY)
     test_fused_backward(cuda, oracle, shape, gpu.LEAKY, False)
 
