@@ -36,7 +36,6 @@ dnb_status cuda_fail(cudaError_t e, const char *what, const char *file, int line
 // Device-side error word bits (DeviceState::error_word).
 enum : unsigned {
     DEVERR_WAIT_BARRIER = 1u,  // a CTA gave up waiting for the other CTAs of its grid
-    DEVERR_WAIT_COPY = 2u,     // a CTA gave up waiting for its own bulk copy
     DEVERR_WAIT_PEER = 4u,     // gave up waiting for another GPU
 };
 
@@ -297,11 +296,6 @@ __device__ __forceinline__ unsigned long long global_ns() {
     unsigned long long t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
-}
-__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned *p) {
-    unsigned v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
 }
 __device__ __forceinline__ unsigned ld_volatile(const unsigned *p) {
     return *reinterpret_cast<const volatile unsigned *>(p);
