@@ -18,7 +18,8 @@
  *     (src/gpu.zig:48-55,443-449);
  *   - pointers are raw device pointers owned by the caller (Buf{ptr,len} without the
  *     length, src/gpu.zig:117-134). The library owns only its per-stream workspace
- *     (per-channel partials and barrier counters) and the comm state.
+ *     (per-channel partials, the fused kernels' tagged records and launch epoch) and the
+ *     comm state.
  * Threading: calls on one stream must come from one host thread at a time.
  */
 #ifndef DNB200_H
@@ -281,7 +282,9 @@ dnb_status dnb_comm_destroy(dnb_comm comm);
  * sync-BN calls on a communicator, from one host thread per rank. Needs spatial % 4 == 0,
  * 16-byte aligned tensors and filters <= max_channels; DNB_ERR_UNSUPPORTED otherwise (the
  * split entries below then apply). A rank that never makes its call leaves the others'
- * kernels waiting until the wait limit; they return DNB_ERR_TIMEOUT. */
+ * kernels waiting until the wait limit; they return DNB_ERR_TIMEOUT. The records a call
+ * exchanges are tagged with its call number, which repeats after 2^32 - 1 fused calls on one
+ * communicator: recreate the communicator before then. */
 dnb_status dnb_syncbn_act_forward_train(dnb_comm comm, const float *x, float *y, float *x_norm, int64_t batch,
                                         int64_t filters, int64_t spatial, const float *scales, const float *biases,
                                         float *mean, float *variance, float *rolling_mean,
