@@ -19,7 +19,8 @@ hundreds of MB of traffic earlier and each kernel also writes back its predecess
 outputs, as in a training step; the launches of a region run back to back between one
 pair of CUDA events on the launching stream (a GPU-side spin before the region lets the
 host queue them all first). `--flush read|write` instead runs an untimed read (or write)
-of a 256 MiB buffer before each launch and brackets every launch with its own events.
+of a 256 MiB buffer before each launch and brackets every launch with its own events;
+`--flush none` gives the warm-L2 figure (one tensor set, back-to-back launches).
 `ms_per_step` is the step region's time per step, the kernel figures come from the other
 two; a barrier and a synchronize bracket each region and the times are the maximum over
 ranks. `value` is the algorithmic bytes of all ranks (20 B per element per step) divided
@@ -65,11 +66,12 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--shape", default="128,128,32,32", help="per-GPU batch,channels,height,width")
-    ap.add_argument("--flush", choices=["rotate", "read", "write"], default="rotate",
+    ap.add_argument("--flush", choices=["rotate", "read", "write", "none"], default="rotate",
                     help="cold L2 for every timed kernel: rotate through sets of tensors larger than L2 "
                          "together, with no flush kernel (each kernel also writes back the previous "
                          "one's dirty outputs, as in a training step); or read a 256 MiB buffer before "
-                         "each kernel (L2 left clean); or write one (L2 left full of dirty lines)")
+                         "each kernel (L2 left clean); or write one (L2 left full of dirty lines). "
+                         "'none' is the warm-L2 figure: the same tensors every launch, back to back")
     ap.add_argument("--syncbn", choices=["fused", "split"], default="fused",
                     help="N > 1: statistics exchanged inside the fused kernels over NVLink (fused) or by "
                          "NCCL collectives between split kernels (split)")
@@ -223,6 +225,7 @@ def run_ours(a):
     # rotate: enough sets of (x, delta, y, dx) that a step's tensors were last touched more
     # than two L2 capacities (2 x 126 MB) of traffic earlier
     n_sets = 1 if a.flush != "rotate" else max(2, -(-(3 * 126 * 2**20) // (4 * E * 4)) + 1)
+    back_to_back = a.flush in ("rotate", "none")
     sets = []
     for _ in range(n_sets):
         sx = torch.randn(E, generator=g, device=dev)
@@ -232,7 +235,7 @@ def run_ours(a):
     gamma = torch.rand(C, generator=g, device=dev) + 0.5
     beta = torch.randn(C, generator=g, device=dev) * 0.1
     mean, var, rm, rv, bu, su, md, vd = (torch.zeros(C, device=dev) for _ in range(8))
-    flush_buf = torch.ones(64 << 20, dtype=torch.float32, device=dev) if a.flush != "rotate" else None
+    flush_buf = torch.ones(64 << 20, dtype=torch.float32, device=dev) if not back_to_back else None
 
     def flush():
         if a.flush == "read":
@@ -269,7 +272,7 @@ def run_ours(a):
             dist.barrier()
         torch.cuda.synchronize()
         torch.cuda._sleep(int(0.25e-3 * 2e9) * a.steps)
-        if a.flush == "rotate":
+        if back_to_back:
             # back-to-back launches between one pair of events
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(stream)
@@ -291,12 +294,12 @@ def run_ours(a):
     clocks = ClockSampler(local)
     clocks.start()
     launches0 = gpu.launch_count()
-    if a.flush == "rotate":
+    if back_to_back:
         ms_step = timed(lambda k: (fwd(k), bwd(k)))
     launches = gpu.launch_count() - launches0
     ms_fwd = timed(fwd)
     ms_bwd = timed(bwd)
-    if a.flush != "rotate":
+    if not back_to_back:
         ms_step = ms_fwd + ms_bwd
         launches = gpu.launch_count() - launches0  # K forward + K backward launches
     if dist:
@@ -344,6 +347,8 @@ def run_ours(a):
                    "l2": (f"rotating {n_sets} sets of (x, delta, y, dx), {n_sets * 4 * E * 4 / 2**20:.0f} MiB "
                           f"> 2 x 126 MB L2: every kernel starts cold and writes back its predecessor's "
                           f"outputs" if a.flush == "rotate" else
+                          "warm L2: the same (x, delta, y, dx) every launch, back to back (not the "
+                          "headline)" if a.flush == "none" else
                           f"256 MiB buffer {'read' if a.flush == 'read' else 'written'} before every timed "
                           f"kernel (cold L2{'' if a.flush == 'read' else ', full of dirty lines'})")
                          + f"; {E * 4 / 2**20:.0f} MiB tensors",
