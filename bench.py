@@ -1,41 +1,52 @@
-"""Benchmark: fused batchnorm + leaky forward and backward (BASELINE configs 0 and 1;
-config 4's sync-BN across GPUs when N > 1).
+"""Benchmark: one data-parallel training step of a batchnorm + leaky layer
+by default (config 0+1 with --config 01).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--shape B,C,H,W]
+                    [--config 4|01] [--shape B,C,H,W] [--sgd-weights N]
 
-A step is one training pass of one BN + leaky(0.1) layer over one batch:
-    forward  dnb_bn_act_forward_train  (read x, write y: 8 B/elem compulsory)
-    backward dnb_bn_act_backward       (read delta and x, write dx: 12 B/elem compulsory)
-on NCHW fp32 [128,128,32,32] per GPU (16.8 M elements, 64 MiB per tensor). With N > 1 GPUs
-every rank holds its own 128-image shard and the per-channel statistics are combined
-across ranks each step (sync-BN, global batch 128*N): weak scaling.
+A step (config 4, per GPU):
+    forward  sync-BN + leaky(0.1) train forward   (read x, write y: 8 B/elem compulsory)
+    backward sync-BN + leaky backward             (read delta and x, write dx: 12 B/elem)
+    update   SGD momentum 0.9, decay 5e-4         (read w and wu, write both: 16 B/weight)
+on NCHW fp32 [128,256,28,28] per GPU (25.7 M elements, 98 MiB per tensor) and a 64 Mi-float
+weight vector. With N GPUs every rank holds its own 128-image shard and the per-channel
+statistics span all ranks (sync-BN, global batch 128*N; the fused kernels exchange them over
+NVLink themselves): weak scaling. N = 1 runs the same step on one GPU (the single-GPU fused
+kernels). `--config 01` is BASELINE configs 0+1: [128,128,32,32], forward + backward, no
+update.
 
-Timing: W untimed steps, then three timed regions of K launches each: K whole steps
-(forward on set k, backward on set k+1), K forwards, K backwards. Every kernel starts with
-a cold L2: by default the launches rotate through 3 sets of (x, delta, y, dx) (768 MiB at
-the default shape, more than twice the 126 MB L2), so a launch's tensors were last touched
-hundreds of MB of traffic earlier and each kernel also writes back its predecessor's dirty
-outputs, as in a training step; the launches of a region run back to back between one
-pair of CUDA events on the launching stream (a GPU-side spin before the region lets the
-host queue them all first). `--flush read|write` instead runs an untimed read (or write)
-of a 256 MiB buffer before each launch and brackets every launch with its own events;
-`--flush none` gives the warm-L2 figure (one tensor set, back-to-back launches).
-`ms_per_step` is the step region's time per step, the kernel figures come from the other
-two; a barrier and a synchronize bracket each region and the times are the maximum over
-ranks. `value` is the algorithmic bytes of all ranks (20 B per element per step) divided
-by the step time.
+Before timing, every rank runs one step and checks it (`parity` in the line): the global
+per-channel mean and variance against a float64 recomputation over all ranks' shards
+(1e-5 relative / 1e-6 absolute, relative to max(|exact|, the terms' 2-norm / n)); mean,
+variance and rolling statistics bit-identical on every rank; y and dx bit-identical to a
+float32 recomputation from the kernels' own per-channel values (numpy, one IEEE rounding per
+operation, as the reference's strict-mode CPU code); the backward sums within the same bar
+of float64; SGD bit-exact on a sample of weights (exact rational arithmetic for the fused
+multiply-adds). A failed check prints the line with `parity` = "failed: ..." and exits 1.
 
-`e2e` repeats the step through the C ABI with HOST buffers: x and delta are copied in
-from pinned memory and y and dx copied out every step, inside the timed region.
+Timing: W untimed steps, then timed regions of K launches each: K whole steps (forward on
+set k, backward on set k+1, then the update), K forwards, K backwards, K updates. Every
+kernel starts with a cold L2: the launches rotate through sets of (x, delta, y, dx) that
+together exceed twice the 126 MB L2 and the weight vectors are 512 MiB, so each kernel also
+writes back its predecessor's dirty outputs, as in a training step. The launches of a region
+run back to back between one pair of CUDA events on the launching stream (a GPU-side spin
+before the region lets the host queue them all first); a barrier and a synchronize bracket
+each region and the times are the maximum over ranks. `--flush read|write` instead runs an
+untimed read (or write) of a 256 MiB buffer before each launch and brackets every launch with
+its own events; `--flush none` gives the warm-L2 figure (one tensor set, back to back).
+`value` is the algorithmic bytes of all ranks per step divided by the step time.
+
+`e2e` repeats the step through the C ABI with HOST buffers: x and delta are copied in from
+pinned memory and y and dx copied out every step, inside the timed region (the weights stay
+resident on the device, as in training).
 
 `--impl reference` times the reference's CPU implementation of the same step (the C
-restatement of blas.zig / batchnorm.zig / activations.zig in oracle/, the reference's own
-Zig code having no toolchain here) on all host cores. Where a GPU and the reference's own
-kernel file built for sm_100a (oracle/_ref/libref_gpu.so) are present, its line also carries
-`gpu_kernels`: the reference's unfused GPU layer sequences (12 launches forward, 7 backward,
-with the reference's grids) timed on the same workload the same way as this library's step,
-and its 3-launch SGD weight update on 64 Mi weights.
+restatement of blas.zig / batchnorm.zig / activations.zig / convolutional.zig's update in
+oracle/, the reference's own Zig code having no toolchain here) on all host cores. Where a
+GPU and the reference's own kernel file built for sm_100a (oracle/_ref/libref_gpu.so) are
+present, its line also carries `gpu_kernels`: the reference's unfused GPU layer sequences (12
+launches forward, 7 backward, 3 for the update, with the reference's grids) timed on the same
+workload the same way as this library's step.
 """
 from __future__ import annotations
 
@@ -47,6 +58,7 @@ import subprocess
 import sys
 import threading
 import time
+from fractions import Fraction
 
 import numpy as np
 
@@ -56,16 +68,26 @@ sys.path.insert(0, ROOT)
 LEAKY = 7
 BYTES_FWD = 8   # per element: read x, write y
 BYTES_BWD = 12  # per element: read delta, read x, write dx
+BYTES_SGD = 16  # per weight: read w, wu; write w, wu
 HBM_NOMINAL_GBS = 8000.0  # BASELINE metric's "% of 8 TB/s"
+SGD_LR, SGD_MOMENTUM, SGD_DECAY = 0.1, 0.9, 5e-4
+
+CONFIGS = {
+    "4": {"shape": (128, 256, 28, 28), "sgd_weights": 64 << 20},
+    "01": {"shape": (128, 128, 32, 32), "sgd_weights": 0},
+}
 
 
-def parse():
+def parse(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--shape", default="128,128,32,32", help="per-GPU batch,channels,height,width")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="4",
+                    help="BASELINE config: 4 = sync-BN step + SGD (default), 01 = BN forward + backward")
+    ap.add_argument("--shape", default="", help="per-GPU batch,channels,height,width (overrides the config's)")
+    ap.add_argument("--sgd-weights", type=int, default=-1, help="weights of the SGD update (0: no update)")
     ap.add_argument("--flush", choices=["rotate", "read", "write", "none"], default="rotate",
                     help="cold L2 for every timed kernel: rotate through sets of tensors larger than L2 "
                          "together, with no flush kernel (each kernel also writes back the previous "
@@ -81,16 +103,33 @@ def parse():
     ap.add_argument("--op", default="", help="with --ops: only the ops whose name contains this")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    a = ap.parse_args()
+    ap.add_argument("--no-parity", action="store_true", help="skip the pre-timing parity check")
+    a = ap.parse_args(argv)
     a.warmup = max(a.warmup, 3)
-    a.shape = tuple(int(v) for v in a.shape.split(","))
+    cfg = CONFIGS[a.config]
+    a.shape = tuple(int(v) for v in a.shape.split(",")) if a.shape else cfg["shape"]
+    a.sgd_weights = cfg["sgd_weights"] if a.sgd_weights < 0 else a.sgd_weights
     return a
 
 
-def workload_desc(shape, n):
-    B, C, H, W = shape
-    return (f"BASELINE cfg0+cfg1: BN-train forward + leaky(0.1) then BN+leaky backward, NCHW fp32 "
-            f"[{B},{C},{H},{W}] per GPU" + (f"; sync-BN over {n} GPUs (global batch {B * n})" if n > 1 else ""))
+def workload_desc(a, n):
+    B, C, H, W = a.shape
+    if a.config == "4":
+        head = "BASELINE cfg4: data-parallel sync-BN training step"
+    else:
+        head = "BASELINE cfg0+cfg1: BN-train forward + leaky(0.1) then BN+leaky backward"
+    s = (f"{head}, NCHW fp32 [{B},{C},{H},{W}] per GPU, global batch {B * n}"
+         + (f", per-channel statistics synchronised over {n} GPUs" if n > 1 else ", 1 GPU")
+         + "; sync-BN+leaky(0.1) forward, backward")
+    if a.sgd_weights:
+        s += (f", then SGD (momentum {SGD_MOMENTUM}, decay {SGD_DECAY}, lr {SGD_LR}) on "
+              f"{a.sgd_weights / 2**20:.0f} Mi fp32 weights per GPU")
+    return s
+
+
+def step_bytes(a, E):
+    """Algorithmic bytes of one rank's step."""
+    return (BYTES_FWD + BYTES_BWD) * E + BYTES_SGD * a.sgd_weights
 
 
 def measured_peaks():
@@ -102,7 +141,7 @@ def measured_peaks():
 
 
 def profiled_traffic():
-    """dram bytes per launch of the backward kernel from the committed ncu summary."""
+    """ncu DRAM bytes per launch of the kernels, from the committed summary."""
     p = os.path.join(ROOT, "profiles", "bn_traffic.json")
     if os.path.exists(p):
         try:
@@ -115,8 +154,8 @@ def profiled_traffic():
 # ---- clocks ---------------------------------------------------------------------------
 
 class ClockSampler:
-    """SM clock and clock-event reasons sampled every ~2 ms through NVML (read-only queries)
-    from a background thread while the timed region runs; nvidia-smi once as a fallback."""
+    """SM clock and clock-event reasons sampled every ~1 ms through NVML (read-only queries)
+    from a background thread while the timed regions run; nvidia-smi once as a fallback."""
 
     REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
                ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
@@ -162,7 +201,7 @@ class ClockSampler:
                 self.samples.append((sm, bits))
             except Exception:
                 break
-            time.sleep(0.002)
+            time.sleep(0.001)
 
     def stop(self):
         if self.nvml is None:
@@ -181,8 +220,8 @@ class ClockSampler:
             for name, const in self.REASONS:
                 if bits & getattr(n, const, 0):
                     reasons.add(name)
-        return {"sm_mhz": statistics.median(s for s, _ in self.samples), "sm_max_mhz": smax,
-                "reasons": sorted(reasons), "samples": len(self.samples), "source": "nvml"}
+        return {"sm_mhz": statistics.median(s for s, _ in self.samples), "sm_min_mhz": min(s for s, _ in self.samples),
+                "sm_max_mhz": smax, "reasons": sorted(reasons), "samples": len(self.samples), "source": "nvml"}
 
     def _smi_once(self):
         try:
@@ -192,6 +231,155 @@ class ClockSampler:
             return {"sm_mhz": sm, "sm_max_mhz": smax, "reasons": [], "samples": 1, "source": "nvidia-smi after"}
         except Exception:
             return None
+
+
+# ---- parity of one step (plain numpy / torch float64 checker; not the library) -------------
+
+def round_f32(v: Fraction) -> np.float32:
+    """The float32 nearest to the rational v, ties to even."""
+    f = np.float32(float(v))
+    best = None
+    for c in (np.nextafter(f, np.float32(-np.inf)), f, np.nextafter(f, np.float32(np.inf))):
+        if not np.isfinite(c):
+            continue
+        err = abs(Fraction(float(c)) - v)
+        key = (err, int(np.array(c).view(np.uint32)) & 1)
+        if best is None or key < best[0]:
+            best = (key, c)
+    return best[1]
+
+
+def fma_f32(a, b, c) -> np.float32:
+    """fmaf(a, b, c) with a single rounding."""
+    return round_f32(Fraction(float(a)) * Fraction(float(b)) + Fraction(float(c)))
+
+
+def leaky_f32(t):
+    return np.where(t > np.float32(0), t, np.float32(0.1) * t)
+
+
+def check_step_parity(dist, world, B, C, S, x, delta, y, dx, gamma, beta, mean, var, rm0, rv0, rm, rv, bu, su, md, vd,
+                      w0, wu0, w, wu, sgd_batch):
+    """Checks one step's results on this rank (see the module docstring). Returns
+    (ok, detail); every rank takes the same collective steps in the same order."""
+    import torch
+
+    f32 = np.float32
+    fails = []
+    n_total = B * S * world
+    # global statistics in float64 over every rank's shard
+    xd = x.view(B, C, S).double()
+    s1 = xd.sum(dim=(0, 2))
+    sq = (xd * xd).sum(dim=(0, 2))
+    if dist:
+        dist.all_reduce(s1)
+        dist.all_reduce(sq)
+    mu = s1 / n_total
+    dev2 = (xd - mu[None, :, None]) ** 2
+    m2 = dev2.sum(dim=(0, 2))
+    q = (dev2 * dev2).sum(dim=(0, 2))
+    del dev2, xd
+    if dist:
+        dist.all_reduce(m2)
+        dist.all_reduce(q)
+    var_exact = m2 / (n_total - 1)
+
+    def close(got, want, scale, name):
+        got = got.double()
+        bound = 1e-6 + 1e-5 * torch.maximum(want.abs(), scale)
+        err = (got - want).abs()
+        plain = float((err / want.abs().clamp_min(1e-30)).max())
+        if bool((err > bound).any()):
+            fails.append(f"{name}: max err/bound {float((err / bound).max()):.3g}")
+        return plain
+
+    rel = {"mean": close(mean, mu, sq.sqrt() / n_total, "mean"),
+           "variance": close(var, var_exact, q.sqrt() / (n_total - 1), "variance")}
+    # the statistics and rolling statistics are identical on every rank
+    if dist:
+        mine = torch.cat([mean, var, rm, rv]).view(torch.int32)
+        allv = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(allv, mine)
+        if any(not torch.equal(v, allv[0]) for v in allv):
+            fails.append("per-channel statistics differ between ranks")
+    m = mean.cpu().numpy()
+    v = var.cpu().numpy()
+    rm_w = np.array([fma_f32(f32(1) - f32(0.99), m[c], rm0[c] * f32(0.99)) for c in range(C)], f32)
+    rv_w = np.array([fma_f32(f32(1) - f32(0.99), v[c], rv0[c] * f32(0.99)) for c in range(C)], f32)
+    if not (np.array_equal(rm.cpu().numpy().view(np.uint32), rm_w.view(np.uint32))
+            and np.array_equal(rv.cpu().numpy().view(np.uint32), rv_w.view(np.uint32))):
+        fails.append("rolling statistics not bit-exact")
+    # per-element outputs from the kernels' per-channel values, in slabs of images
+    g = gamma.cpu().numpy()[None, :, None]
+    b = beta.cpu().numpy()[None, :, None]
+    inv = (f32(1) / (np.sqrt(v) + f32(0.000001)))[None, :, None]
+    inv2 = (f32(1) / np.sqrt(v + f32(0.00001)))[None, :, None]
+    mdv = md.cpu().numpy()
+    vdv = vd.cpu().numpy()[None, :, None]
+    denom = f32(n_total)
+    mdd = (mdv / denom)[None, :, None]
+    mc = m[None, :, None]
+    g1 = np.zeros(C, np.float64)
+    g2 = np.zeros(C, np.float64)
+    g1s = np.zeros(C, np.float64)
+    g2s = np.zeros(C, np.float64)
+    y_bad = dx_bad = 0
+    step = max(1, (1 << 22) // (C * S))
+    for n0 in range(0, B, step):
+        n1 = min(B, n0 + step)
+        xs = x.view(B, C, S)[n0:n1].cpu().numpy()
+        ds = delta.view(B, C, S)[n0:n1].cpu().numpy()
+        yw = leaky_f32((xs - mc) * inv * g + b)
+        y_bad += int((y.view(B, C, S)[n0:n1].cpu().numpy().view(np.uint32) != yw.view(np.uint32)).sum())
+        gr = ds * np.where(yw > f32(0), f32(1), f32(0.1))
+        dxw = (gr * g) * inv2 + (vdv * f32(2) * (xs - mc)) / denom + mdd
+        dx_bad += int((dx.view(B, C, S)[n0:n1].cpu().numpy().view(np.uint32) != dxw.view(np.uint32)).sum())
+        gd = gr.astype(np.float64)
+        t2 = gd * (xs.astype(np.float64) - mc.astype(np.float64))
+        g1 += gd.sum(axis=(0, 2))
+        g2 += t2.sum(axis=(0, 2))
+        g1s += (gd * gd).sum(axis=(0, 2))
+        g2s += (t2 * t2).sum(axis=(0, 2))
+    if y_bad:
+        fails.append(f"y: {y_bad} elements not bit-exact")
+    if dx_bad:
+        fails.append(f"dx: {dx_bad} elements not bit-exact")
+    sums = torch.from_numpy(np.stack([g1, g2, g1s, g2s])).to(x.device)
+    if dist:
+        dist.all_reduce(sums)
+    s_g, s_gx, s_gs, s_gxs = (t for t in sums)
+    rel["bias_updates"] = close(bu, s_g, s_gs.sqrt(), "bias_updates (sum g)")
+    inv_t = torch.from_numpy(inv.ravel().astype(np.float64)).to(x.device)
+    rel["scale_updates"] = close(su, s_gx * inv_t, s_gxs.sqrt() * inv_t, "scale_updates (sum g x_norm)")
+    # SGD: exact fused multiply-adds on a sample of weights
+    if w0 is not None:
+        b32 = f32(sgd_batch)
+        a_decay = f32(-f32(SGD_DECAY) * b32)
+        a_lr = f32(f32(SGD_LR) / b32)
+        rng = np.random.default_rng(7)
+        idx = np.sort(rng.choice(w.numel(), size=2048, replace=False))
+        it = torch.from_numpy(idx).to(w.device)
+        w_got = w[it].cpu().numpy()
+        u_got = wu[it].cpu().numpy()
+        bad = 0
+        for k in range(idx.size):
+            u1 = fma_f32(a_decay, w0[k], wu0[k])
+            w1 = fma_f32(a_lr, u1, w0[k])
+            u2 = f32(u1 * f32(SGD_MOMENTUM))
+            bad += int(np.float32(w1).view(np.uint32) != w_got[k].view(np.uint32)
+                       or np.float32(u2).view(np.uint32) != u_got[k].view(np.uint32))
+        if bad:
+            fails.append(f"sgd: {bad} of {idx.size} sampled weights not bit-exact")
+    ok = torch.tensor([0 if fails else 1], device=x.device)
+    if dist:
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    detail = {"max_rel_err_vs_exact": {k: float(f"{v:.3g}") for k, v in rel.items()},
+              "checked": "global mean/variance vs float64 over all ranks; statistics identical on every rank; "
+                         "rolling statistics, y, dx bit-exact; backward sums vs float64"
+                         + ("; SGD bit-exact on 2048 sampled weights" if w0 is not None else "")}
+    if fails:
+        detail["rank_failures"] = fails
+    return bool(ok.item()), detail
 
 
 # ---- our implementation -----------------------------------------------------------------
@@ -219,6 +407,8 @@ def run_ours(a):
     B, C, H, W = a.shape
     S = H * W
     E = B * C * S
+    NW = a.sgd_weights
+    sgd_batch = B * world
     dev = torch.device("cuda", local)
     g = torch.Generator(device=dev)
     g.manual_seed(1234 + rank)
@@ -234,7 +424,14 @@ def run_ours(a):
     x, delta, y, dx = sets[0]
     gamma = torch.rand(C, generator=g, device=dev) + 0.5
     beta = torch.randn(C, generator=g, device=dev) * 0.1
-    mean, var, rm, rv, bu, su, md, vd = (torch.zeros(C, device=dev) for _ in range(8))
+    mean, var, bu, su, md, vd = (torch.zeros(C, device=dev) for _ in range(6))
+    rm = torch.randn(C, generator=g, device=dev) * 0.5
+    rv = torch.rand(C, generator=g, device=dev) * 1.5 + 0.5
+    # the weights are replicated: the same values on every rank
+    gw = torch.Generator(device=dev)
+    gw.manual_seed(99)
+    wts = torch.randn(NW, generator=gw, device=dev) * 0.01 if NW else None
+    wup = torch.randn(NW, generator=gw, device=dev) * 1e-3 if NW else None
     flush_buf = torch.ones(64 << 20, dtype=torch.float32, device=dev) if not back_to_back else None
 
     def flush():
@@ -255,12 +452,45 @@ def run_ours(a):
         sx, sd, sy, sdx = sets[(k + 1) % n_sets]
         layer.backward(sx, sd, sdx, gamma, beta, mean, var, bu, su, md, vd, LEAKY)
 
+    def sgd(k):
+        if NW:
+            gpu.sgdMomentum(NW, wts, wup, SGD_LR, SGD_MOMENTUM, SGD_DECAY, sgd_batch)
+
+    def whole(k):
+        fwd(k)
+        bwd(k)
+        sgd(k)
+
+    # one checked step on set 0 (forward and backward on the same tensors, as a layer does)
+    parity = "skipped (--no-parity)"
+    parity_detail = None
+    if not a.no_parity:
+        rm0, rv0 = rm.cpu().numpy(), rv.cpu().numpy()
+        w0 = wu0 = None
+        if NW:
+            rs = np.random.default_rng(7)
+            idx = np.sort(rs.choice(NW, size=2048, replace=False))
+            it = torch.from_numpy(idx).to(dev)
+            w0, wu0 = wts[it].cpu().numpy(), wup[it].cpu().numpy()
+        bu.zero_()
+        su.zero_()
+        layer.forward(x, y, gamma, beta, mean, var, rm, rv, LEAKY)
+        layer.backward(x, delta, dx, gamma, beta, mean, var, bu, su, md, vd, LEAKY)
+        sgd(0)
+        torch.cuda.synchronize()
+        gpu.check_device_error()
+        ok, parity_detail = check_step_parity(dist, world, B, C, S, x, delta, y, dx, gamma, beta, mean, var, rm0, rv0,
+                                              rm, rv, bu, su, md, vd, w0, wu0, wts, wup, sgd_batch)
+        parity = "ok" if ok else "failed: " + "; ".join(parity_detail.get("rank_failures", ["on another rank"]))
+
     stream = torch.cuda.current_stream()
     for k in range(a.warmup):
         flush()
         fwd(k)
         flush()
         bwd(k)
+        flush()
+        sgd(k)
     torch.cuda.synchronize()
     gpu.check_device_error()
 
@@ -273,7 +503,6 @@ def run_ours(a):
         torch.cuda.synchronize()
         torch.cuda._sleep(int(0.25e-3 * 2e9) * a.steps)
         if back_to_back:
-            # back-to-back launches between one pair of events
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(stream)
             for k in range(a.steps):
@@ -281,7 +510,6 @@ def run_ours(a):
             e1.record(stream)
             torch.cuda.synchronize()
             return e0.elapsed_time(e1) / a.steps
-        # a flush kernel before every launch: one pair of events per launch
         ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(a.steps)]
         for k in range(a.steps):
             flush()
@@ -295,25 +523,26 @@ def run_ours(a):
     clocks.start()
     launches0 = gpu.launch_count()
     if back_to_back:
-        ms_step = timed(lambda k: (fwd(k), bwd(k)))
+        ms_step = timed(whole)
     launches = gpu.launch_count() - launches0
     ms_fwd = timed(fwd)
     ms_bwd = timed(bwd)
+    ms_sgd = timed(sgd) if NW else 0.0
     if not back_to_back:
-        ms_step = ms_fwd + ms_bwd
-        launches = gpu.launch_count() - launches0  # K forward + K backward launches
+        ms_step = ms_fwd + ms_bwd + ms_sgd
+        launches = gpu.launch_count() - launches0
     if dist:
         dist.barrier()
     clk = clocks.stop()
     gpu.check_device_error()
     if dist:
-        t = torch.tensor([ms_step, ms_fwd, ms_bwd], device=dev)
+        t = torch.tensor([ms_step, ms_fwd, ms_bwd, ms_sgd], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms_step, ms_fwd, ms_bwd = (float(v) for v in t.cpu())
+        ms_step, ms_fwd, ms_bwd, ms_sgd = (float(v) for v in t.cpu())
 
     e2e = None
     if not a.no_e2e:
-        e2e = run_e2e(a, layer, x, y, delta, dx, gamma, beta, mean, var, rm, rv, bu, su, md, vd, dev, dist, world)
+        e2e = run_e2e(a, layer, x, y, delta, dx, gamma, beta, mean, var, rm, rv, bu, su, md, vd, sgd, dev, dist, world)
 
     torch.cuda.synchronize()
     layer.close()
@@ -322,15 +551,29 @@ def run_ours(a):
         dist.barrier()
         dist.destroy_process_group()
     if rank != 0:
+        if parity.startswith("failed"):
+            raise SystemExit(1)
         return
     peak, peak_kind = measured_peaks()
-    bytes_step = (BYTES_FWD + BYTES_BWD) * E * world
+    bytes_step = step_bytes(a, E) * world
     value = bytes_step / (ms_step * 1e-3) / 1e9
-    bwd_gbs = BYTES_BWD * E / (ms_bwd * 1e-3) / 1e9
-    fwd_gbs = BYTES_FWD * E / (ms_fwd * 1e-3) / 1e9
-    traffic = profiled_traffic()
+    traffic = profiled_traffic() or {}
+    kernels = {
+        "bn_act_forward_train": (ms_fwd, BYTES_FWD * E, "sync-BN+leaky forward" if world > 1 else "BN+leaky forward"),
+        "bn_act_backward": (ms_bwd, BYTES_BWD * E, "sync-BN+leaky backward" if world > 1 else "BN+leaky backward"),
+    }
+    if NW:
+        kernels["sgd_momentum"] = (ms_sgd, BYTES_SGD * NW, "fused SGD update")
+    kout = {}
+    for name, (ms, nbytes, what) in kernels.items():
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        kout[name] = {"what": what, "ms": round(ms, 5), "GBps": round(gbs, 1), "frac_of_peak": round(gbs / peak, 4),
+                      "algorithmic_bytes": nbytes, "launches": 1}
+    dom = max(kernels, key=lambda k: kernels[k][0])
+    dms, dbytes, _ = kernels[dom]
+    dgbs = dbytes / (dms * 1e-3) / 1e9
     line = {
-        "metric": "fused BN+leaky forward+backward HBM throughput (algorithmic bytes / device time)",
+        "metric": "training-step HBM throughput of the BN+leaky layer (algorithmic bytes / device time)",
         "value": round(value, 2),
         "unit": "GB/s",
         "n_gpus": world,
@@ -341,45 +584,47 @@ def run_ours(a):
         "scaling": "weak",
         "vs_baseline": None,
         "dtype": "f32",
-        "data": "synthetic (torch.randn / rand, seeded per rank)",
-        "config": {"workload": workload_desc(a.shape, world), "batch_per_gpu": B, "channels": C, "hw": [H, W],
-                   "global_batch": B * world, "activation": "leaky 0.1",
-                   "l2": (f"rotating {n_sets} sets of (x, delta, y, dx), {n_sets * 4 * E * 4 / 2**20:.0f} MiB "
-                          f"> 2 x 126 MB L2: every kernel starts cold and writes back its predecessor's "
-                          f"outputs" if a.flush == "rotate" else
+        "data": "synthetic (torch.randn / rand, seeded per rank; weights identical on every rank)",
+        "parity": parity,
+        "config": {"workload": workload_desc(a, world), "baseline_config": a.config, "batch_per_gpu": B,
+                   "channels": C, "hw": [H, W], "global_batch": B * world, "activation": "leaky 0.1",
+                   "sgd_weights_per_gpu": NW,
+                   "l2": (f"rotating {n_sets} sets of (x, delta, y, dx), {n_sets * 4 * E * 4 / 2**20:.0f} MiB, "
+                          f"and {2 * NW * 4 / 2**20:.0f} MiB of weights: every kernel starts cold and writes back "
+                          f"its predecessor's outputs" if a.flush == "rotate" else
                           "warm L2: the same (x, delta, y, dx) every launch, back to back (not the "
                           "headline)" if a.flush == "none" else
                           f"256 MiB buffer {'read' if a.flush == 'read' else 'written'} before every timed "
                           f"kernel (cold L2{'' if a.flush == 'read' else ', full of dirty lines'})")
                          + f"; {E * 4 / 2**20:.0f} MiB tensors",
                    "parallelism": f"dp{world}" + (f" + sync-BN ({a.syncbn})" if world > 1 else "")},
+        "bytes_per_step_per_gpu": step_bytes(a, E),
         "elems_per_s": round(E * world / (ms_step * 1e-3), 1),
         "pct_of_8TBs": round(100.0 * value / world / HBM_NOMINAL_GBS, 2),
-        "kernels": {
-            "bn_act_forward_train": {"ms": round(ms_fwd, 5), "GBps": round(fwd_gbs, 1),
-                                     "frac_of_peak": round(fwd_gbs / peak, 4), "bytes_per_elem": BYTES_FWD},
-            "bn_act_backward": {"ms": round(ms_bwd, 5), "GBps": round(bwd_gbs, 1),
-                                "frac_of_peak": round(bwd_gbs / peak, 4), "bytes_per_elem": BYTES_BWD},
-        },
-        "roofline": {"kernel": "bn_act_backward", "bound": "hbm", "achieved": round(bwd_gbs, 1), "peak": peak,
+        "kernels": kout,
+        "roofline": {"kernel": dom, "bound": "hbm", "achieved": round(dgbs, 1), "peak": peak,
                      "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
-                     else "fallback 6.65 TB/s", "unit": "GB/s", "frac": round(bwd_gbs / peak, 4),
-                     "traffic": (traffic or {}).get("bwd_dram_bytes_per_launch"),
-                     "algorithmic_bytes": BYTES_BWD * E},
+                     else "fallback 6.65 TB/s", "unit": "GB/s", "frac": round(dgbs / peak, 4),
+                     "traffic": (traffic.get(dom) or {}).get("dram_bytes_per_launch"),
+                     "algorithmic_bytes": dbytes},
         "gpu_launches": launches,
         "clocks": clk,
     }
+    if parity_detail:
+        line["parity_detail"] = parity_detail
     if e2e:
         line["e2e"] = e2e
     if not a.no_cpu_baseline and world == 1:
         line["cpu_baseline"] = cpu_baseline(a, threads=1)
     print(json.dumps(line), flush=True)
+    if parity.startswith("failed"):
+        raise SystemExit(1)
 
 
-def run_e2e(a, layer, x, y, delta, dx, gamma, beta, mean, var, rm, rv, bu, su, md, vd, dev, dist, world):
+def run_e2e(a, layer, x, y, delta, dx, gamma, beta, mean, var, rm, rv, bu, su, md, vd, sgd, dev, dist, world):
     """The step through the C ABI with host buffers: every step copies its x and delta in
-    from pinned host memory, runs the forward and backward, and copies y and dx back out,
-    all inside the timed region. Copies in, kernels and copies out run on three streams
+    from pinned host memory, runs the forward, backward and update, and copies y and dx back
+    out, all inside the timed region. Copies in, kernels and copies out run on three streams
     over two device buffer sets, so step k's outputs travel to the host while step k+1's
     inputs travel in (PCIe is full duplex) and step k+1 computes; the time is from the
     first copy in to the last copy out."""
@@ -412,6 +657,7 @@ def run_e2e(a, layer, x, y, delta, dx, gamma, beta, mean, var, rm, rv, bu, su, m
         with torch.cuda.stream(s_run):
             layer.forward(bx, by, gamma, beta, mean, var, rm, rv, LEAKY)
             layer.backward(bx, bd, bdx, gamma, beta, mean, var, bu, su, md, vd, LEAKY)
+            sgd(k)
         ev_run[b].record(s_run)
         s_out.wait_event(ev_run[b])
         with torch.cuda.stream(s_out):
@@ -435,25 +681,30 @@ def run_e2e(a, layer, x, y, delta, dx, gamma, beta, mean, var, rm, rv, bu, su, m
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
-    value = (BYTES_FWD + BYTES_BWD) * E * world / (ms * 1e-3) / 1e9
+    value = step_bytes(a, E) * world / (ms * 1e-3) / 1e9
     return {"value": round(value, 2), "unit": "GB/s", "ms_per_step": round(ms, 4), "steps": steps,
             "h2d_bytes_per_step": 2 * E * 4, "d2h_bytes_per_step": 2 * E * 4,
             "path": "C ABI with pinned host buffers; copies in, kernels and copies out on three streams over "
-                    "two device buffer sets (steps pipelined)"}
+                    "two device buffer sets (steps pipelined); weights resident on the device"}
 
 
 # ---- the reference's CPU implementation -----------------------------------------------------
 
-def cpu_step_sample(shape, threads, steps, warmup):
-    """Times the reference's op sequence (oracle restatement) for one BN+leaky training step."""
+def cpu_step_sample(a, threads, steps, warmup, images=None):
+    """Times the reference's op sequence (oracle restatement) for one training step of the
+    workload: BN+leaky forward and backward over `images` images of the per-GPU shape (all
+    of them by default), then the SGD update of the config's weights. Returns (seconds per
+    step, elements, weights)."""
     from darknet_zig_b200 import synth
     from oracle.oracle import Oracle
 
     orc = Oracle()
     orc.set_threads(threads)
-    B, C, H, W = shape
+    B, C, H, W = a.shape
+    B = images or B
     S = H * W
     E = B * C * S
+    NW = a.sgd_weights
     x = synth.normal(1, (E,), 0, 1)
     d0 = synth.normal(2, (E,), 0, 1)
     gamma = synth.uniform(3, (C,), 0.5, 1.5)
@@ -463,16 +714,20 @@ def cpu_step_sample(shape, threads, steps, warmup):
     xn = np.zeros(E, np.float32)
     z = lambda: np.zeros(C, np.float32)  # noqa: E731
     mean, var, rm, rv, bu, su, md, vd = (z() for _ in range(8))
+    w = synth.normal(5, (NW,), 0, 0.01) if NW else None
+    wu = synth.normal(6, (NW,), 0, 1e-3) if NW else None
     times = []
     for i in range(warmup + steps):
         delta = d0.copy()
         t0 = time.perf_counter()
         orc.bn_forward_layer(x, y, xs, xn, B, C, S, gamma, beta, mean, var, rm, rv, True, LEAKY)
         orc.bn_backward_layer(xs, xn, y, delta, B, C, S, gamma, mean, var, bu, su, md, vd, LEAKY)
+        if NW:
+            orc.sgd_update(w, wu, SGD_LR, SGD_MOMENTUM, SGD_DECAY, B)
         t1 = time.perf_counter()
         if i >= warmup:
             times.append(t1 - t0)
-    return sum(times) / len(times), E
+    return sum(times) / len(times), E, NW
 
 
 def cpu_model() -> str:
@@ -489,14 +744,14 @@ def cpu_model() -> str:
 
 def cpu_baseline(a, threads):
     # a bounded sample: as many full steps as fit ~10 s at this core count (at least 2)
-    t_one, E = cpu_step_sample(a.shape, threads, 1, 0)
+    t_one, E, NW = cpu_step_sample(a, threads, 1, 0)
     steps = int(max(2, min(20, 10.0 / max(t_one, 1e-3))))
-    t, E = cpu_step_sample(a.shape, threads, steps, 1)
-    gbs = (BYTES_FWD + BYTES_BWD) * E / t / 1e9
+    t, E, NW = cpu_step_sample(a, threads, steps, 1)
+    gbs = ((BYTES_FWD + BYTES_BWD) * E + BYTES_SGD * NW) / t / 1e9
     return {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-            "sample": f"{steps} full steps of the workload (BN+leaky fwd+bwd, {E} elements) through the C "
-                      f"restatement of the reference CPU ops; {t * 1e3:.1f} ms/step; host {os.cpu_count()} cpus "
-                      f"({cpu_model()})",
+            "sample": f"{steps} full steps of the workload (BN+leaky fwd+bwd over {E} elements"
+                      + (f", SGD on {NW} weights" if NW else "") + f") through the C restatement of the "
+                      f"reference CPU ops; {t * 1e3:.1f} ms/step; host {os.cpu_count()} cpus ({cpu_model()})",
             "ms_per_step": round(t * 1e3, 2), "elems_per_s": round(E / t, 1)}
 
 
@@ -504,10 +759,11 @@ def ref_gpu_kernels(a):
     """The reference's GPU path on this box's GPU 0: darknet_kernels.hip compiled for sm_100a
     with the reference's flags, launched with the reference's grids (oracle/ref_gpu.cu). One
     step = the conv-layer BN + leaky forward sequence (convolutional.zig:263-268,
-    batchnorm.zig:129-153) and backward sequence (convolutional.zig:279-282,
-    batchnorm.zig:155-170). Timed like this library's step: rotating tensor sets larger than
-    L2 together, K back-to-back steps between one pair of events after W warm-up steps.
-    Returns None when there is no GPU or the library was not built."""
+    batchnorm.zig:129-153), backward sequence (convolutional.zig:279-282,
+    batchnorm.zig:155-170) and the weight update (convolutional.zig:332-334). Timed like this
+    library's step: rotating tensor sets larger than L2 together, K back-to-back steps
+    between one pair of events after W warm-up steps. Returns None when there is no GPU or
+    the library was not built."""
     try:
         import torch
     except ImportError:
@@ -524,6 +780,7 @@ def ref_gpu_kernels(a):
     B, C, H, W = a.shape
     S = H * W
     E = B * C * S
+    NW = a.sgd_weights
     g = torch.Generator(device="cuda")
     g.manual_seed(4321)
     # per set: the conv output (forward in place), the saved x and x_norm, delta (backward in place)
@@ -532,6 +789,8 @@ def ref_gpu_kernels(a):
     gamma = torch.rand(C, generator=g, device="cuda") + 0.5
     beta = torch.randn(C, generator=g, device="cuda") * 0.1
     mean, var, rm, rv, bu, su, md, vd = (torch.zeros(C, device="cuda") for _ in range(8))
+    w = torch.randn(NW, generator=g, device="cuda") * 0.01 if NW else None
+    wu = torch.randn(NW, generator=g, device="cuda") * 1e-3 if NW else None
     stream = torch.cuda.current_stream()
     sh = stream.cuda_stream
     P = lambda t: t.data_ptr()  # noqa: E731
@@ -545,6 +804,10 @@ def ref_gpu_kernels(a):
         out, xs, xn, delta = sets[(k + 1) % n_sets]
         ref.conv_bn_backward(P(out), P(delta), P(xs), P(xn), P(mean), P(var), P(gamma), P(bu), P(su), P(md), P(vd),
                              B, C, S, LEAKY, sh)
+
+    def sgd(k):
+        if NW:
+            ref.sgd_weights(NW, SGD_LR, SGD_MOMENTUM, SGD_DECAY, B, P(w), P(wu), sh)
 
     def timed(body, steps):
         torch.cuda.synchronize()
@@ -560,36 +823,25 @@ def ref_gpu_kernels(a):
     for k in range(a.warmup):
         fwd(k)
         bwd(k)
+        sgd(k)
     torch.cuda.synchronize()
-    ms_step = timed(lambda k: (fwd(k), bwd(k)), a.steps)
+    ms_step = timed(lambda k: (fwd(k), bwd(k), sgd(k)), a.steps)
     ms_fwd = timed(fwd, a.steps)
     ms_bwd = timed(bwd, a.steps)
-    del sets
-    # SGD weight update of BASELINE config 4: 64 Mi weights, 3 launches (axpy, axpy, scal)
-    nw = 64 << 20
-    wsets = [(torch.randn(nw, generator=g, device="cuda") * 0.01, torch.randn(nw, generator=g, device="cuda") * 1e-3)
-             for _ in range(2)]
-
-    def sgd(k):
-        w, wu = wsets[k % 2]
-        ref.sgd_weights(nw, 0.1, 0.9, 5e-4, 1024, P(w), P(wu), sh)
-
-    for k in range(a.warmup):
-        sgd(k)
-    ms_sgd = timed(sgd, a.steps)
-    del wsets
+    ms_sgd = timed(sgd, a.steps) if NW else 0.0
+    del sets, w, wu
     torch.cuda.empty_cache()
     gbs = lambda nbytes, ms: round(nbytes / (ms * 1e-3) / 1e9, 1)  # noqa: E731
     return {
         "what": "the reference's darknet_kernels.hip built for sm_100a (nvcc -O3, its build.zig flags), "
-                "launched with its own grids (gpu.zig:420-477) on GPU 0 of this box",
+                "launched with its own grids (gpu.zig:420-477) on GPU 0 of this box, 1 GPU",
         "ms_per_step": round(ms_step, 5),
-        "value": gbs((BYTES_FWD + BYTES_BWD) * E, ms_step),
-        "unit": "GB/s (this workload's algorithmic bytes, 20 B/elem, / device time)",
+        "value": gbs(step_bytes(a, E), ms_step),
+        "unit": "GB/s (this workload's algorithmic bytes / device time)",
         "forward_ms": round(ms_fwd, 5),
         "backward_ms": round(ms_bwd, 5),
-        "launches_per_step": ref.launches_forward + ref.launches_backward,
-        "sgd_64Mi": {"ms": round(ms_sgd, 5), "GBps": gbs(16 * nw, ms_sgd), "launches": ref.launches_sgd},
+        "sgd_ms": round(ms_sgd, 5),
+        "launches_per_step": ref.launches_forward + ref.launches_backward + (ref.launches_sgd if NW else 0),
         "l2": f"rotating {n_sets} sets of 4 tensors ({n_sets * 4 * E * 4 / 2**20:.0f} MiB)",
     }
 
@@ -601,11 +853,11 @@ def run_reference(a):
     threads = os.cpu_count() or 1
     B, C, H, W = a.shape
     gpu_kernels = ref_gpu_kernels(a)
-    t, E = cpu_step_sample(a.shape, threads, a.steps, a.warmup)
-    gbs = (BYTES_FWD + BYTES_BWD) * E / t / 1e9
+    t, E, NW = cpu_step_sample(a, threads, a.steps, min(a.warmup, 3))
+    gbs = ((BYTES_FWD + BYTES_BWD) * E + BYTES_SGD * NW) / t / 1e9
     line = {
         "impl": "reference",
-        "metric": "fused BN+leaky forward+backward HBM throughput (algorithmic bytes / device time)",
+        "metric": "training-step HBM throughput of the BN+leaky layer (algorithmic bytes / device time)",
         "value": round(gbs, 3),
         "unit": "GB/s",
         "n_gpus": a.gpus,
@@ -617,12 +869,14 @@ def run_reference(a):
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic (seeded splitmix64 generator)",
-        "config": {"workload": workload_desc(a.shape, 1), "batch_per_gpu": B, "channels": C, "hw": [H, W],
-                   "parallelism": "host cores (reference CPU ops, OpenMP over channels)"},
+        "config": {"workload": workload_desc(a, 1), "baseline_config": a.config, "batch_per_gpu": B, "channels": C,
+                   "hw": [H, W], "sgd_weights_per_gpu": NW,
+                   "parallelism": "host cores (reference CPU ops, OpenMP over channels / elements)"},
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-                         "sample": f"{a.steps} full steps (after {a.warmup} warm-up) of the reference op sequence "
-                                   f"batchnorm.zig:74-123 + activations.zig, C restatement in oracle/; "
-                                   f"{threads} threads of {cpu_model()}"},
+                         "sample": f"{a.steps} full steps (after {min(a.warmup, 3)} warm-up) of the reference op "
+                                   f"sequence batchnorm.zig:74-123 + activations.zig"
+                                   + (" + convolutional.zig:217-233's update" if NW else "")
+                                   + f", C restatement in oracle/; {threads} threads of {cpu_model()}"},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "elems_per_s": round(E / t, 1),
     }
@@ -656,18 +910,20 @@ def run_ops(a):
             run(sets[k % n_sets])
         torch.cuda.synchronize()
         torch.cuda._sleep(int(0.1e-3 * 2e9) * steps)
+        l0 = gpu.launch_count()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         for k in range(steps):
             run(sets[k % n_sets])
         e1.record(stream)
         torch.cuda.synchronize()
+        launches = (gpu.launch_count() - l0) / steps
         gpu.check_device_error()
         us = e0.elapsed_time(e1) / steps * 1e3
         gbs = nbytes / (us * 1e-6) / 1e9
         print(json.dumps({"op": name, "config": config, "us": round(us, 2), "GBps": round(gbs, 1),
                           "frac_of_peak": round(gbs / peak, 4), "algorithmic_bytes": int(nbytes),
-                          "rotating_sets": n_sets}), flush=True)
+                          "launches_per_call": launches, "rotating_sets": n_sets}), flush=True)
 
     f32 = dict(dtype=torch.float32, device="cuda")
     LEAKY_ = LEAKY
@@ -714,19 +970,21 @@ def run_ops(a):
     timed("sgd_momentum", "cfg4 64 Mi weights, lr 0.1 momentum 0.9 decay 5e-4 batch 1024", 16 * n,
           lambda i: (torch.randn(n, **f32) * 0.01, torch.randn(n, **f32) * 1e-3),
           lambda t: gpu.sgdMomentum(n, t[0], t[1], 0.1, 0.9, 5e-4, 1024))
-    E = 128 * 256 * 784
+    for (b_, c_, s_, label) in ((128, 256, 784, "cfg4 per GPU 128x256x28x28"), (128, 128, 1024, "cfg0/1 128x128x32x32"),
+                                (64, 1024, 49, "64x1024x7x7"), (16, 40, 169, "16x40x13x13")):
+        E = b_ * c_ * s_
 
-    def make_bnt(i):
-        return (torch.randn(E, **f32), torch.empty(E, **f32), torch.randn(E, **f32), torch.empty(E, **f32),
-                torch.rand(256, **f32) + 0.5, torch.randn(256, **f32) * 0.1,
-                *(torch.zeros(256, **f32) for _ in range(8)))
+        def make_bnt(i, E=E, c_=c_):
+            return (torch.randn(E, **f32), torch.empty(E, **f32), torch.randn(E, **f32), torch.empty(E, **f32),
+                    torch.rand(c_, **f32) + 0.5, torch.randn(c_, **f32) * 0.1,
+                    *(torch.zeros(c_, **f32) for _ in range(8)))
 
-    timed("bn_act_forward_train", "cfg4 per GPU 128x256x28x28 leaky", 8 * E, make_bnt,
-          lambda t: gpu.bnActForwardTrain(t[0], t[1], None, 128, 256, 784, t[4], t[5], t[6], t[7], t[8], t[9],
-                                          LEAKY_))
-    timed("bn_act_backward", "cfg4 per GPU 128x256x28x28 leaky", 12 * E, make_bnt,
-          lambda t: gpu.bnActBackward(t[0], None, t[2], t[3], 128, 256, 784, t[4], t[5], t[6], t[7], t[10], t[11],
-                                      t[12], t[13], LEAKY_))
+        timed("bn_act_forward_train", f"{label} leaky", 8 * E, make_bnt,
+              lambda t, b_=b_, c_=c_, s_=s_: gpu.bnActForwardTrain(t[0], t[1], None, b_, c_, s_, t[4], t[5], t[6],
+                                                                   t[7], t[8], t[9], LEAKY_))
+        timed("bn_act_backward", f"{label} leaky", 12 * E, make_bnt,
+              lambda t, b_=b_, c_=c_, s_=s_: gpu.bnActBackward(t[0], None, t[2], t[3], b_, c_, s_, t[4], t[5], t[6],
+                                                               t[7], t[10], t[11], t[12], t[13], LEAKY_))
     # the BLAS-1 basics on 64 Mi floats
     timed("fill", "64 Mi floats", 4 * n, lambda i: (torch.empty(n, **f32),), lambda t: gpu.fill(t[0], n, 0.5))
     timed("copy", "64 Mi floats", 8 * n, lambda i: (torch.randn(n, **f32), torch.empty(n, **f32)),

@@ -26,6 +26,8 @@
 // statistics the outputs are bit-identical to it.
 #include <math.h>
 
+#include <atomic>
+
 #include "dnb_chan.cuh"
 
 namespace dnb {
@@ -1344,18 +1346,23 @@ dnb_status run_sweep(int64_t batch, int64_t filters, int64_t spatial, int act, P
     DNB_TRY(current_device(&ds));
     return dispatch_act(act, [&]<int A>() -> dnb_status {
         auto kern = k_bn_sweep<BWD, A, HASY>;
-        // CTAs one SM holds with up to 16 KB of dynamic shared memory (a plan needs less
-        // unless its shares are thousands of units long; checked again below)
-        static int occupancy = -1;
-        if (occupancy < 0) DNB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occupancy, kern, kSThreads, 16384));
+        // CTAs one SM holds with up to 16 KB of dynamic shared memory, per device (a plan
+        // needs less unless its shares are thousands of units long; larger plans are
+        // refused below, so the default dynamic shared-memory limit always suffices and
+        // no per-device attribute is set). Cached as occupancy + 1; concurrent first calls
+        // store the same value.
+        static std::atomic<int> occ_by_device[kMaxDevices];
+        int occ1 = occ_by_device[ds->device].load(std::memory_order_relaxed);
+        if (occ1 == 0) {
+            int o = 0;
+            DNB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, kern, kSThreads, 16384));
+            occ1 = o + 1;
+            occ_by_device[ds->device].store(occ1, std::memory_order_relaxed);
+        }
+        const int occupancy = occ1 - 1;
         if (occupancy < 1) return DNB_OK;
         const PPlan pl = plan_sweep<BWD, HASY>(batch, filters, spatial, ds, occupancy);
         if (!pl.ok || pl.smem > 16384) return DNB_OK;
-        static size_t smem_set = 0;
-        if (pl.smem > smem_set) {
-            DNB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem));
-            smem_set = pl.smem;
-        }
         Workspace *ws = nullptr;
         DNB_TRY(workspace(stream, 0, &ws, (size_t)pl.G * pl.P * 2 * 4));
         fill_partition(a, pl, batch, filters, spatial);

@@ -39,6 +39,8 @@ enum : unsigned {
     DEVERR_WAIT_PEER = 4u,     // gave up waiting for another GPU
 };
 
+constexpr int kMaxDevices = 64;  // device ordinals the per-device state covers
+
 struct DeviceState {
     int device = -1;
     int sm_count = 0;
@@ -90,6 +92,8 @@ dnb_status after_launch(cudaStream_t stream, const char *what);
 void note_launch();
 // Spin limit for device-side waits, in nanoseconds.
 unsigned long long wait_limit_ns();
+// True under dnb_set_sync_after_launch(1).
+bool sync_after_launch();
 
 inline cudaStream_t as_stream(dnb_stream s) { return reinterpret_cast<cudaStream_t>(s); }
 inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }

@@ -263,6 +263,20 @@ dnb_status noalloc_scratch(float **out) {
     return DNB_OK;
 }
 
+// after_launch without its device lookup: counts the launch, checks it, and under
+// dnb_set_sync_after_launch(1) synchronises the stream and reports a fault here (the
+// device-side wait word is not read: these kernels do not wait on one another).
+dnb_status noalloc_after_launch(cudaStream_t s, const char *what) {
+    note_launch();
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(DNB_ERR_CUDA, "launching %s failed: %s", what, cudaGetErrorString(e));
+    if (sync_after_launch()) {
+        e = cudaStreamSynchronize(s);
+        if (e != cudaSuccess) return fail(DNB_ERR_CUDA, "%s faulted: %s", what, cudaGetErrorString(e));
+    }
+    return DNB_OK;
+}
+
 }  // namespace
 }  // namespace dnb
 
@@ -304,13 +318,10 @@ extern "C" dnb_status dnb_mean_noalloc(const float *x, int64_t batch, int64_t fi
         // the previous call's partials are still there: clear the slots this call reads
         DNB_CUDA(cudaMemsetAsync(partial, 0, sizeof(float) * (size_t)(filters * chunks), s));
     }
-    note_launch();
-    DNB_CUDA(cudaGetLastError());
+    DNB_TRY(noalloc_after_launch(s, what));
     const float scale = 1.0f / (float)(batch * spatial);  // blas.zig:107
     const unsigned warps_per_block = 8;
     const unsigned blocks = (unsigned)((filters + warps_per_block - 1) / warps_per_block);
     k_chan_close<<<blocks, 32 * warps_per_block, 0, s>>>(filters, g.chunks, partial, Close::Mean, scale, nullptr, out);
-    note_launch();
-    DNB_CUDA(cudaGetLastError());
-    return DNB_OK;
+    return noalloc_after_launch(s, what);
 }

@@ -19,14 +19,14 @@ namespace {
 
 thread_local char g_detail[512] = "";
 std::mutex g_mu;
-DeviceState g_dev[64];
+DeviceState g_dev[kMaxDevices];
 std::map<std::pair<int, cudaStream_t>, Workspace *> g_ws;
 std::atomic<unsigned long long> g_launches{0};
 bool g_sync_after_launch = false;
 unsigned long long g_wait_limit_ns = 2000ull * 1000ull * 1000ull;  // 2 s
 
 dnb_status init_device(int device) {
-    if (device < 0 || device >= 64) return fail(DNB_ERR_INVALID, "device index %d out of range", device);
+    if (device < 0 || device >= kMaxDevices) return fail(DNB_ERR_INVALID, "device index %d out of range", device);
     DeviceState &ds = g_dev[device];
     if (ds.device == device) return DNB_OK;
     DNB_CUDA(cudaSetDevice(device));
@@ -136,6 +136,8 @@ dnb_status after_launch(cudaStream_t stream, const char *what) {
 }
 
 unsigned long long wait_limit_ns() { return g_wait_limit_ns; }
+
+bool sync_after_launch() { return g_sync_after_launch; }
 
 }  // namespace dnb
 

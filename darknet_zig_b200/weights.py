@@ -120,6 +120,13 @@ def save(path: str, layers: list[LayerParams], seen: int = 0) -> None:
                 f.write(np.ascontiguousarray(a, dtype="<f4").tobytes())
 
 
+def _read_bytes(f, n: int, path: str, what: str) -> bytes:
+    buf = f.read(n)
+    if len(buf) != n:
+        raise EOFError(f"{path}: file ends inside {what} ({len(buf)} of {n} bytes)")
+    return buf
+
+
 def _read(f, a: np.ndarray, path: str) -> None:
     want = a.size * 4
     buf = f.read(want)
@@ -141,9 +148,9 @@ def load(path: str, layers: list[LayerParams], start: int = 0, cutoff: int | Non
             raise EOFError(f"{path}: no weights header")
         major, minor, _revision = struct.unpack("<iii", head)
         if major * 10 + minor >= 2 and major < 1000 and minor < 1000:
-            (seen,) = struct.unpack("<Q", f.read(8))
+            (seen,) = struct.unpack("<Q", _read_bytes(f, 8, path, "the 64-bit seen count"))
         else:
-            (seen,) = struct.unpack("<i", f.read(4))
+            (seen,) = struct.unpack("<i", _read_bytes(f, 4, path, "the 32-bit seen count"))
             seen = max(0, seen)
         transpose = major > 1000 or minor > 1000
         end = len(layers) if cutoff is None else min(cutoff, len(layers))

@@ -18,6 +18,7 @@ so no multiply-add is fused behind the restatement's back.
 """
 from __future__ import annotations
 
+import json
 import os
 import subprocess
 import sys
@@ -27,8 +28,26 @@ BUILD = os.path.join(HERE, "_build")
 REF_OUT = os.path.join(HERE, "_ref")
 ORACLE_SO = os.path.join(BUILD, "liboracle.so")
 REF_EMU_SO = os.path.join(REF_OUT, "libref_emulate.so")
-REFERENCE_KERNELS = os.environ.get(
-    "DNB_REFERENCE_KERNELS", "/root/reference/src/kernels/darknet_kernels.hip")
+
+
+def _reference_kernels() -> str:
+    """The reference's kernel file: $DNB_REFERENCE_KERNELS, else src/kernels/darknet_kernels.hip
+    under $DNB_REFERENCE_ROOT, else under the `reference_path` that BASELINE.json (the
+    repository's build setting for the reference checkout) names. "" when none is set."""
+    path = os.environ.get("DNB_REFERENCE_KERNELS")
+    if path:
+        return path
+    root = os.environ.get("DNB_REFERENCE_ROOT")
+    if not root:
+        try:
+            with open(os.path.join(os.path.dirname(HERE), "BASELINE.json")) as f:
+                root = json.load(f).get("reference_path") or ""
+        except (OSError, ValueError):
+            root = ""
+    return os.path.join(root, "src", "kernels", "darknet_kernels.hip") if root else ""
+
+
+REFERENCE_KERNELS = _reference_kernels()
 
 CFLAGS = ["-O3", "-march=x86-64-v3", "-ffp-contract=off", "-fno-fast-math", "-fPIC", "-shared"]
 
@@ -53,7 +72,7 @@ def build_oracle(force: bool = False) -> str:
 def build_ref_emulation(force: bool = False) -> str | None:
     """Compile the reference's own kernel file for the host. Returns None when the
     reference tree is not mounted (e.g. on the GPU box, which uses the prebuilt file)."""
-    if not os.path.exists(REFERENCE_KERNELS):
+    if not REFERENCE_KERNELS or not os.path.exists(REFERENCE_KERNELS):
         return REF_EMU_SO if os.path.exists(REF_EMU_SO) else None
     src = os.path.join(HERE, "ref_emulate.cpp")
     shim = os.path.join(HERE, "hip_host_shim.h")
@@ -74,7 +93,7 @@ def build_ref_gpu(force: bool = False) -> str | None:
     it with `nvcc -x cu -O3 -arch=...` (build.zig:144-156), so this keeps nvcc's default
     contraction and precision flags. Returns None when neither the reference tree nor a
     prebuilt file is present."""
-    if not os.path.exists(REFERENCE_KERNELS):
+    if not REFERENCE_KERNELS or not os.path.exists(REFERENCE_KERNELS):
         return REF_GPU_SO if os.path.exists(REF_GPU_SO) else None
     src = os.path.join(HERE, "ref_gpu.cu")
     os.makedirs(REF_OUT, exist_ok=True)

@@ -18,6 +18,22 @@ def pytest_configure(config):
     config.addinivalue_line("markers", "slow: full BASELINE-size case")
 
 
+def pytest_terminal_summary(terminalreporter):
+    """The plain |exact|-relative error of every reduction checked against the terms'
+    2-norm bar (parity.py), worst case per check, beside the fraction of the bar it used."""
+    try:
+        from parity import PLAIN_REL
+    except ImportError:
+        return
+    if not PLAIN_REL:
+        return
+    tr = terminalreporter
+    tr.write_sep("-", "reductions: worst plain relative error |got-exact|/|exact| (and share of the bar used)")
+    for name in sorted(PLAIN_REL):
+        plain, of_bar = PLAIN_REL[name]
+        tr.write_line(f"{name:40s} plain rel {plain:9.3g}   of bar {of_bar:6.3f}")
+
+
 @pytest.fixture(scope="session")
 def oracle():
     from oracle.oracle import get_oracle

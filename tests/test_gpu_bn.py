@@ -20,6 +20,10 @@ from darknet_zig_b200 import gpu, synth
 from darknet_zig_b200.layers import BatchNorm
 from parity import assert_bitexact, assert_close, channel_view, exact_channel_sum
 
+# bias_updates / scale_updates accumulate into the caller's values: one float32 rounding of
+# a result of magnitude ~1 (the initial values are U(-1, 1)) is up to 6e-8, below this bar
+ACC_ATOL = 1e-6
+
 pytestmark = pytest.mark.gpu
 
 # (batch, filters, spatial): generic path (S % 4 != 0), persistent path at several unit
@@ -152,25 +156,41 @@ def test_fused_backward(cuda, oracle, shape, act, with_y):
                       su, md, vd, act)
     md_h, vd_h = host(md), host(vd)
     g, gs, dx_w = oracle_backward_given_stats(oracle, x, y_h, delta, shape, gamma, m, v, md_h, vd_h, act)
-    if act == gpu.LOGISTIC and not with_y:
-        # y recomputed with CUDA expf on the device vs the stored y here
-        assert_close(host(dxt), dx_w, "dx", rtol=1e-4, atol=1e-5)
-    else:
-        assert_bitexact(host(dxt), dx_w, "dx")
-    # per-channel sums against float64 sums of the same float32 terms
+    # bit-exact for every activation: without y the kernel recomputes y from x with the
+    # forward's own arithmetic (CUDA expf included), so it equals the stored device y
+    assert_bitexact(host(dxt), dx_w, "dx")
+    # per-channel sums against float64 sums of the same float32 terms (bu and su also
+    # carry one float32 rounding of the accumulation into the caller's initial values)
     s1, s1n = exact_channel_sum(g, B, C, S)
-    assert_close(host(bu) - bu0, s1, "bias_updates", atol=1e-5, scale=s1n)
+    assert_close(host(bu) - bu0, s1, "bias_updates", atol=ACC_ATOL, scale=s1n)
     xn = x.copy()
     oracle.normalize(xn, m, v, B, C, S)
     s2, s2n = exact_channel_sum(g * xn, B, C, S)
-    assert_close(host(su) - su0, s2, "scale_updates", atol=1e-5, scale=s2n)
+    assert_close(host(su) - su0, s2, "scale_updates", atol=ACC_ATOL, scale=s2n)
     inv = (-1.0 / np.sqrt(v.astype(np.float32) + np.float32(1e-5))).astype(np.float64)
     sgs, sgsn = exact_channel_sum(gs, B, C, S)
-    assert_close(md_h, sgs * inv, "mean_delta", atol=1e-5, scale=sgsn * np.abs(inv))
+    assert_close(md_h, sgs * inv, "mean_delta", scale=sgsn * np.abs(inv))
     fac = -0.5 * (v.astype(np.float64) + 1e-5) ** -1.5
     xm = (x.reshape(B, C, S) - m[None, :, None]).ravel().astype(np.float32)
     svd, svdn = exact_channel_sum(gs * xm, B, C, S)
-    assert_close(vd_h, svd * fac, "variance_delta", atol=1e-5, scale=svdn * np.abs(fac))
+    assert_close(vd_h, svd * fac, "variance_delta", scale=svdn * np.abs(fac))
+
+
+def backward_sum_scales(oracle, x, y, delta, gamma, m, v, shape, act):
+    """Per-channel 2-norms of the terms behind bias_updates, scale_updates, mean_delta and
+    variance_delta (the scale of the reduction bar, parity.py)."""
+    B, C, S = shape
+    g = delta.copy()
+    oracle.gradient_array(y, act, g)
+    gs = g.copy()
+    oracle.scale_bias(gs, gamma, B, C, S)
+    xn = x.copy()
+    oracle.normalize(xn, m, v, B, C, S)
+    xm = (x.reshape(B, C, S) - m[None, :, None]).ravel().astype(np.float32)
+    inv = 1.0 / np.sqrt(v.astype(np.float64) + 1e-5)
+    fac = 0.5 * (v.astype(np.float64) + 1e-5) ** -1.5
+    return {"bu": exact_channel_sum(g, B, C, S)[1], "su": exact_channel_sum(g * xn, B, C, S)[1],
+            "md": exact_channel_sum(gs, B, C, S)[1] * inv, "vd": exact_channel_sum(gs * xm, B, C, S)[1] * fac}
 
 
 @pytest.mark.slow
@@ -251,25 +271,25 @@ def test_standalone_reductions(cuda, oracle, shape):
     out = dev(bu0)
     gpu.backwardBias(out, dev(delta), B, C, S)
     s, sn = exact_channel_sum(delta, B, C, S)
-    assert_close(host(out) - bu0, s, "backward_bias", atol=1e-5, scale=sn)
+    assert_close(host(out) - bu0, s, "backward_bias", atol=1e-6, scale=sn)
 
     out = dev(bu0)
     gpu.backwardScale(dev(xn), dev(delta), B, C, S, out)
     s, sn = exact_channel_sum(delta * xn, B, C, S)
-    assert_close(host(out) - bu0, s, "backward_scale", atol=1e-5, scale=sn)
+    assert_close(host(out) - bu0, s, "backward_scale", atol=1e-6, scale=sn)
 
     out = torch.zeros(C, device="cuda")
     gpu.meanDelta(dev(delta), dev(rv), B, C, S, out)
     s, sn = exact_channel_sum(delta, B, C, S)
     f = (np.float32(-1) / np.sqrt(rv + np.float32(1e-5))).astype(np.float64)
-    assert_close(host(out), s * f, "mean_delta", atol=1e-5, scale=sn * np.abs(f))
+    assert_close(host(out), s * f, "mean_delta", atol=1e-6, scale=sn * np.abs(f))
 
     out = torch.zeros(C, device="cuda")
     gpu.varianceDelta(dev(x), dev(delta), dev(mean), dev(rv), B, C, S, out)
     xm = (x.reshape(B, C, S) - mean[None, :, None]).ravel().astype(np.float32)
     s, sn = exact_channel_sum(delta * xm, B, C, S)
     f = -0.5 * (rv.astype(np.float64) + 1e-5) ** -1.5
-    assert_close(host(out), s * f, "variance_delta", atol=1e-5, scale=sn * np.abs(f))
+    assert_close(host(out), s * f, "variance_delta", atol=1e-6, scale=sn * np.abs(f))
 
 
 @pytest.mark.parametrize("shape", [(4, 17, 53), (8, 16, 64), (16, 40, 196)])
@@ -291,13 +311,15 @@ def test_unfused_reference_sequence_matches_fused(cuda, oracle, shape):
                                                    bu=bn.bias_updates, su=bn.scale_updates, md=bn.mean_delta,
                                                    vd=bn.variance_delta).items()})
     f, u = layers
-    for k in ("y", "mean", "variance", "rm", "rv"):
-        assert_close(f[k], u[k], k, rtol=1e-5, atol=1e-5)
-    for k in ("bu", "su", "md", "vd", "dx"):
-        assert_close(f[k], u[k], k, rtol=1e-4, atol=1e-4)
+    for k in ("y", "mean", "variance", "rm", "rv", "dx"):
+        assert_close(f[k], u[k], k)
+    # the reductions: relative to the per-channel terms' 2-norm, as every reduction here
+    sc = backward_sum_scales(oracle, x, f["y"], delta, gamma, f["mean"], f["variance"], shape, gpu.LEAKY)
+    for k in ("bu", "su", "md", "vd"):
+        assert_close(f[k], u[k], k, scale=sc[k])
 
 
-def test_syncbn_split_path_two_shards_on_one_gpu(cuda):
+def test_syncbn_split_path_two_shards_on_one_gpu(cuda, oracle):
     """Split sync-BN API: two half-batch shards, partials combined as an all-gather would,
     give the statistics and outputs of the whole batch in one shard."""
     from darknet_zig_b200._lib import call
@@ -322,10 +344,10 @@ def test_syncbn_split_path_two_shards_on_one_gpu(cuda):
         call("syncbn_forward_apply", xi.data_ptr(), y.data_ptr(), None, h, C, S, gathered.data_ptr(), 2,
              g_d.data_ptr(), b_d.data_ptr(), m.data_ptr(), v.data_ptr(), rm.data_ptr(), rv.data_ptr(), gpu.LEAKY,
              stream)
-        assert_close(host(m), host(m_full), "sync mean", rtol=1e-5, atol=1e-6)
-        assert_close(host(v), host(v_full), "sync variance", rtol=1e-5, atol=1e-6)
+        assert_close(host(m), host(m_full), "sync mean")
+        assert_close(host(v), host(v_full), "sync variance")
         half = slice(i * h * C * S, (i + 1) * h * C * S)
-        assert_close(host(y), host(y_full)[half], "sync y", rtol=1e-5, atol=1e-5)
+        assert_close(host(y), host(y_full)[half], "sync y")
     # backward: partial sums of both shards, summed as an all-reduce would
     d_d = dev(delta)
     ds = [d_d[: h * C * S], d_d[h * C * S:]]
@@ -337,17 +359,19 @@ def test_syncbn_split_path_two_shards_on_one_gpu(cuda):
     dx_full = torch.empty_like(y_full)
     bu, su, md, vd = (torch.zeros(C, device="cuda") for _ in range(4))
     gpu.bnActBackward(dev(x), None, d_d, dx_full, B, C, S, g_d, b_d, m_full, v_full, bu, su, md, vd, gpu.LEAKY)
+    sc = backward_sum_scales(oracle, x, host(y_full), delta, gamma, host(m_full), host(v_full), (B, C, S),
+                             gpu.LEAKY)
     for i, (xi, di) in enumerate(zip(xs, ds)):
         dx = torch.empty(h * C * S, device="cuda")
         bu2, su2, md2, vd2 = (torch.zeros(C, device="cuda") for _ in range(4))
         call("syncbn_backward_apply", xi.data_ptr(), None, di.data_ptr(), dx.data_ptr(), h, C, S, B * S,
              red.data_ptr(), g_d.data_ptr(), b_d.data_ptr(), m_full.data_ptr(), v_full.data_ptr(), bu2.data_ptr(),
              su2.data_ptr(), md2.data_ptr(), vd2.data_ptr(), gpu.LEAKY, stream)
-        for got, want, name in ((bu2, bu, "bias_updates"), (su2, su, "scale_updates"), (md2, md, "mean_delta"),
-                                (vd2, vd, "variance_delta")):
-            assert_close(host(got), host(want), f"sync {name}", rtol=1e-5, atol=1e-5)
+        for got, want, name, k in ((bu2, bu, "bias_updates", "bu"), (su2, su, "scale_updates", "su"),
+                                   (md2, md, "mean_delta", "md"), (vd2, vd, "variance_delta", "vd")):
+            assert_close(host(got), host(want), f"sync {name}", scale=sc[k])
         half = slice(i * h * C * S, (i + 1) * h * C * S)
-        assert_close(host(dx), host(dx_full)[half], "sync dx", rtol=1e-4, atol=1e-5)
+        assert_close(host(dx), host(dx_full)[half], "sync dx")
 
 
 def test_rolling_statistics_survive_a_weights_round_trip(cuda, tmp_path):

@@ -218,7 +218,7 @@ def test_softmax_and_cross_entropy(cuda, oracle, rows, classes):
     assert_close(host(d2), wd, "fused delta", rtol=1e-5, atol=1e-6)
     assert_close(host(e2), we, "fused err", rtol=1e-5, atol=1e-6)
     want_cost = oracle.sum_array(we)
-    assert_close(host(cost), np.array([want_cost], np.float32), "cost", rtol=1e-5, atol=1e-5)
+    assert_close(host(cost), np.array([want_cost], np.float32), "cost")
 
 
 @pytest.mark.parametrize("temp,stride,groups", [(2.0, 1, 1), (1.0, 1, 3), (1.0, 2, 2), (0.5, 3, 3)])

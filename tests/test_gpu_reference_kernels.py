@@ -138,10 +138,10 @@ def test_backward_matches_reference_gpu_sequence(ref_gpu, shape):
     n_su = np.sqrt(((gv * xnv) ** 2).sum(axis=1))
     n_md = n_bu * gam * inv
     n_vd = np.sqrt(((gv * xm) ** 2).sum(axis=1)) * gam * 0.5 * (v + 1e-5) ** -1.5
-    assert_close(host(bu), host(bu_r), "bias_updates", atol=1e-5, scale=n_bu)
-    assert_close(host(su), host(su_r), "scale_updates", atol=1e-5, scale=n_su)
-    assert_close(host(md), host(md_r), "mean_delta", atol=1e-5, scale=n_md)
-    assert_close(host(vd), host(vd_r), "variance_delta", atol=1e-5, scale=n_vd)
+    assert_close(host(bu), host(bu_r), "bias_updates", atol=1e-6, scale=n_bu)
+    assert_close(host(su), host(su_r), "scale_updates", atol=1e-6, scale=n_su)
+    assert_close(host(md), host(md_r), "mean_delta", atol=1e-6, scale=n_md)
+    assert_close(host(vd), host(vd_r), "variance_delta", atol=1e-6, scale=n_vd)
     # dx = g*gamma*inv + vd*2(x-mu)/n + md/n: bound by the magnitude of the three terms
     n = B * S
     md_h, vd_h = host(md_r).astype(np.float64), host(vd_r).astype(np.float64)
