@@ -70,7 +70,7 @@ constexpr size_t kSyncWords = 2;
 // rank's exchange buffer of tagged records, 64-bit words
 // [2 parities][kMaxSweepGroups][world][pmax CTAs][2 segments][4].
 constexpr int kMaxRanks = 8;
-constexpr int kMaxSweepGroups = 16;
+constexpr int kMaxSweepGroups = 64;
 struct CommView {
     int rank = 0, world = 1;
     unsigned tag = 0;  // the call number (never 0): the records' tag; parity = tag & 1

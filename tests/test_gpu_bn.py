@@ -41,6 +41,19 @@ SHAPES = [
 FULL_SHAPES = [(128, 128, 1024), (128, 256, 784), (64, 128, 1024)]
 
 
+# The fused entries pick the shared-memory-staged kernel, else the L2 sweep, else the
+# generic multi-launch path; the library reads these switches at every call, so each test
+# below runs each path on the same inputs.
+BN_PATHS = {"stage": {}, "sweep": {"DNB_BN_STAGE": "0"}, "generic": {"DNB_BN_PERSISTENT": "0"}}
+
+
+@pytest.fixture(params=list(BN_PATHS))
+def bn_path(request, monkeypatch):
+    for k, v in BN_PATHS[request.param].items():
+        monkeypatch.setenv(k, v)
+    return request.param
+
+
 def dev(a):
     return torch.from_numpy(np.ascontiguousarray(a)).cuda()
 
@@ -93,7 +106,7 @@ def check_forward_stats(oracle, x, shape, mean_got, var_got):
 
 @pytest.mark.parametrize("shape", SHAPES)
 @pytest.mark.parametrize("act", [gpu.LEAKY, gpu.RELU, gpu.LINEAR, gpu.LOGISTIC])
-def test_fused_forward_train(cuda, oracle, shape, act):
+def test_fused_forward_train(cuda, oracle, shape, act, bn_path):
     B, C, S = shape
     x, gamma, beta, _, rm0, rv0 = make_inputs(shape)
     y = torch.empty(x.size, dtype=torch.float32, device="cuda")
@@ -136,7 +149,7 @@ def oracle_backward_given_stats(oracle, x, y, delta, shape, gamma, mean, var, md
 @pytest.mark.parametrize("shape", SHAPES)
 @pytest.mark.parametrize("act", [gpu.LEAKY, gpu.RELU, gpu.LINEAR, gpu.LOGISTIC])
 @pytest.mark.parametrize("with_y", [False, True])
-def test_fused_backward(cuda, oracle, shape, act, with_y):
+def test_fused_backward(cuda, oracle, shape, act, with_y, bn_path):
     B, C, S = shape
     x, gamma, beta, delta, _, _ = make_inputs(shape, seed=7)
     # forward first (fused) to get the statistics and y the backward uses
@@ -195,18 +208,19 @@ def backward_sum_scales(oracle, x, y, delta, gamma, m, v, shape, act):
 
 @pytest.mark.slow
 @pytest.mark.parametrize("shape", FULL_SHAPES)
-def test_fused_full_size_forward_backward(cuda, oracle, shape):
+def test_fused_full_size_forward_backward(cuda, oracle, shape, bn_path):
     """BASELINE configs 0/1 (128x128x32x32) and 4 (per GPU 128x256x28x28), leaky 0.1, and a
     32 MiB tensor whose forward plan is a single channel group."""
-    test_fused_forward_train(cuda, oracle, shape, gpu.LEAKY)
-    test_fused_backward(cuda, oracle, shape, gpu.LEAKY, False)
+    test_fused_forward_train(cuda, oracle, shape, gpu.LEAKY, bn_path)
+    test_fused_backward(cuda, oracle, shape, gpu.LEAKY, False, bn_path)
 
 
 @pytest.mark.parametrize("shape", [(8, 16, 64), (2, 3, 4), (16, 40, 196), (1, 300, 100), (128, 128, 1024),
-                                   (128, 256, 784)])
+                                   (128, 256, 784), (64, 1024, 49), (16, 40, 169), (4, 17, 53)])
 def test_fused_entries_are_one_launch(cuda, shape):
-    """With spatial % 4 == 0 and aligned tensors each fused entry is a single kernel launch
-    (the persistent kernel), not the multi-launch generic path."""
+    """With aligned tensors each fused entry is a single kernel launch (the staged kernel),
+    not the multi-launch generic path: spatial % 4 == 0, and also spatial % 4 != 0 (7x7,
+    13x13, 53) whenever the element count is a multiple of 4."""
     B, C, S = shape
     x, gamma, beta, delta, rm0, rv0 = make_inputs(shape, seed=5)
     y = torch.empty(x.size, dtype=torch.float32, device="cuda")

@@ -21,7 +21,7 @@ from test_gpu_bn import dev, host, make_inputs
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("shape", [(8, 16, 64), (16, 40, 196), (128, 128, 1024)])
+@pytest.mark.parametrize("shape", [(8, 16, 64), (16, 40, 196), (128, 128, 1024), (128, 256, 784), (16, 40, 169)])
 def test_one_rank_communicator_matches_the_fused_kernels(cuda, shape):
     B, C, S = shape
     comm, handle = gpu.commInit(0, 1, C)
@@ -58,7 +58,7 @@ def test_one_rank_communicator_matches_the_fused_kernels(cuda, shape):
 
 
 def test_unsupported_shape_is_reported(cuda):
-    B, C, S = 4, 6, 9  # spatial % 4 != 0: not taken by the fused kernel
+    B, C, S = 3, 5, 9  # spatial % 4 != 0 and an element count that is not a multiple of 4
     comm, handle = gpu.commInit(0, 1, C)
     try:
         gpu.commConnect(comm, handle)
