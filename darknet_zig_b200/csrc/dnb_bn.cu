@@ -411,6 +411,12 @@ bool persistent_disabled() {
     return e && e[0] == '0';
 }
 
+// DNB_BN_SWEEP=0 turns the L2 sweep off (the staged kernel then takes its shapes).
+bool sweep_disabled() {
+    const char *e = getenv("DNB_BN_SWEEP");
+    return e && e[0] == '0';
+}
+
 // Every CTA owns the same balanced share of each channel group in both passes, and its
 // warps are split by role. The 14 streaming warps reduce the groups (HBM reads) and write
 // the outputs of each group once its parameters are known (the share re-read from L2),
@@ -1126,6 +1132,7 @@ template <bool BWD, bool HASY>
 dnb_status run_sweep(int64_t batch, int64_t filters, int64_t spatial, int act, const BnIO &io, cudaStream_t stream,
                      bool *launched, const char *what, const CommView *cv = nullptr) {
     *launched = false;
+    if (sweep_disabled()) return DNB_OK;
     PArgs a{};
     a.t0 = io.t0;
     a.t1 = io.t1;
@@ -1246,10 +1253,10 @@ dnb_status dnb_bn_act_forward_train(const float *x, float *y, float *x_norm, int
         a.rmean = rolling_mean;
         a.rvar = rolling_variance;
         bool launched = false;
+        DNB_TRY((run_sweep<false, false>(batch, filters, spatial, act, a, s, &launched, what)));
+        if (launched) return DNB_OK;
         if (!stage_disabled()) DNB_TRY((run_stage<false, false>(batch, filters, spatial, act, a, s, &launched, what,
                                                                 nullptr)));
-        if (launched) return DNB_OK;
-        DNB_TRY((run_sweep<false, false>(batch, filters, spatial, act, a, s, &launched, what)));
         if (launched) return DNB_OK;
     }
     const GGeom g = make_ggeom(batch, filters, spatial, aligned16(x));
@@ -1289,17 +1296,16 @@ dnb_status dnb_bn_act_backward(const float *x, const float *y, const float *delt
         a.mean_delta = mean_delta;
         a.var_delta = variance_delta;
         bool launched = false;
-        if (!stage_disabled()) {
-            if (y)
-                DNB_TRY((run_stage<true, true>(batch, filters, spatial, act, a, s, &launched, what, nullptr)));
-            else
-                DNB_TRY((run_stage<true, false>(batch, filters, spatial, act, a, s, &launched, what, nullptr)));
-            if (launched) return DNB_OK;
-        }
         if (y)
             DNB_TRY((run_sweep<true, true>(batch, filters, spatial, act, a, s, &launched, what)));
         else
             DNB_TRY((run_sweep<true, false>(batch, filters, spatial, act, a, s, &launched, what)));
+        if (!launched && !stage_disabled()) {
+            if (y)
+                DNB_TRY((run_stage<true, true>(batch, filters, spatial, act, a, s, &launched, what, nullptr)));
+            else
+                DNB_TRY((run_stage<true, false>(batch, filters, spatial, act, a, s, &launched, what, nullptr)));
+        }
         if (launched) return DNB_OK;
     }
     const GGeom g = make_ggeom(batch, filters, spatial, aligned16(x) && aligned16(delta) && (!y || aligned16(y)));
@@ -1338,10 +1344,9 @@ dnb_status dnb_syncbn_act_forward_train(dnb_comm comm, const float *x, float *y,
     a.rmean = rolling_mean;
     a.rvar = rolling_variance;
     bool launched = false;
-    if (!stage_disabled())
+    DNB_TRY((run_sweep<false, false>(batch, filters, spatial, act, a, as_stream(stream), &launched, what, &cv)));
+    if (!launched && !stage_disabled())
         DNB_TRY((run_stage<false, false>(batch, filters, spatial, act, a, as_stream(stream), &launched, what, &cv)));
-    if (!launched)
-        DNB_TRY((run_sweep<false, false>(batch, filters, spatial, act, a, as_stream(stream), &launched, what, &cv)));
     if (!launched) return fail(DNB_ERR_UNSUPPORTED, "%s: shape not taken by the fused kernel", what);
     return DNB_OK;
 }
@@ -1379,17 +1384,15 @@ dnb_status dnb_syncbn_act_backward(dnb_comm comm, const float *x, const float *y
     a.var_delta = variance_delta;
     bool launched = false;
     const cudaStream_t s = as_stream(stream);
-    if (!stage_disabled()) {
+    if (y)
+        DNB_TRY((run_sweep<true, true>(batch, filters, spatial, act, a, s, &launched, what, &cv)));
+    else
+        DNB_TRY((run_sweep<true, false>(batch, filters, spatial, act, a, s, &launched, what, &cv)));
+    if (!launched && !stage_disabled()) {
         if (y)
             DNB_TRY((run_stage<true, true>(batch, filters, spatial, act, a, s, &launched, what, &cv)));
         else
             DNB_TRY((run_stage<true, false>(batch, filters, spatial, act, a, s, &launched, what, &cv)));
-    }
-    if (!launched) {
-        if (y)
-            DNB_TRY((run_sweep<true, true>(batch, filters, spatial, act, a, s, &launched, what, &cv)));
-        else
-            DNB_TRY((run_sweep<true, false>(batch, filters, spatial, act, a, s, &launched, what, &cv)));
     }
     if (!launched) return fail(DNB_ERR_UNSUPPORTED, "%s: shape not taken by the fused kernel", what);
     return DNB_OK;

@@ -57,6 +57,8 @@ struct TArgs {
     FastDiv f_nk, f_k, f_ps, f_tfull, f_tlast;
     // ring: R slots of nt tensors x SU floats
     int R, SU, slot_floats, vec;
+    int pf_from;     // first group whose share is prefetched into L2 (earlier ones fit the ring)
+    int bulk_out;    // outputs leave by bulk copies from the slot (vec units, no x_norm)
     float denom, inv_denom;
     int denom_pow2;
     BnIO io;
@@ -106,6 +108,28 @@ __device__ __forceinline__ void bulk_load(void *dst, const void *src, unsigned b
         : "memory");
 }
 
+// shared -> global bulk copy (both addresses 16-byte aligned, bytes a multiple of 16), in the
+// issuing thread's current bulk group
+__device__ __forceinline__ void bulk_store(void *dst, const void *src, unsigned bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(smem_addr(src)),
+                 "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// until at most N of this thread's bulk groups still read shared memory
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// until all of this thread's bulk groups are complete (their writes performed)
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// this thread's shared-memory writes, ordered before later bulk copies that read them
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+// bring `bytes` at src (16-byte aligned, a multiple of 16) into L2
+__device__ __forceinline__ void prefetch_l2(const void *src, unsigned bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 template <bool BWD, int A, bool HASY>
 struct Stage {
     static constexpr int NT = BWD ? (HASY ? 3 : 2) : 1;  // input tensors
@@ -119,22 +143,29 @@ struct Stage {
         double2 *lrec;    // [DG][2] merged records
         double *lcnt;     // [DG][2] elements behind the forward's records
         float *ptab;      // [DG][2][8] apply parameters
-        float4 *ctab;     // [DG][2] channel inputs for the closing: (gamma, beta) or (mean, var, gamma, beta)
-        float4 *stab;     // [DG][2] backward: the forward's (mean, inv, gamma, beta) for the statistics
-        int *stats_upto;  // [kTStats] groups whose partials the warp has left
-        int *apply_upto;  // [kTApply] groups whose outputs the warp has written
-        int *ready_upto;  // groups whose apply parameters are in ptab
-        int *published;   // groups whose records the publisher has stored
-        int *stop;        // set when any wait gave up
+        // per-channel inputs of every group's (at most two) share channels, [G][2], loaded once
+        // in the prologue so that no global load sits on the exchange's path:
+        float4 *ctab;     // the closing's inputs: (gamma, beta) or (mean, var, gamma, beta)
+        float4 *stab;     // backward: the forward's (mean, inv, gamma, beta) for the statistics
+        float2 *otab;     // the accumulated outputs' prior values: (rolling mean, rolling variance)
+                          // or (bias_updates, scale_updates)
+        uint64_t *tbar;   // the tables are loaded
+        // per group-state buffer b = g % kTGroupRing, one phase per group using it
+        // (group g waits on phase g / kTGroupRing, parity (g / kTGroupRing) & 1):
+        uint64_t *sbar;  // [DG] every statistics warp has left its partials of the group
+        uint64_t *pbar;  // [DG] the publisher has stored the group's records
+        uint64_t *rbar;  // [DG] the group's apply parameters are in ptab
+        uint64_t *abar;  // [DG] every output warp is done with the group
+        int *stop;       // set when any wait gave up
     };
-    static size_t ctrl_bytes(int R) {
+    static size_t ctrl_bytes(int R, int G) {
         return (size_t)R * 16 +
                (size_t)kTGroupRing * (2 * kTStats * sizeof(float4) + 2 * sizeof(double2) + 2 * sizeof(double) +
-                                      16 * sizeof(float) + 4 * sizeof(float4)) +
-               (kTStats + kTApply + 5) * sizeof(int) + 64;
+                                      16 * sizeof(float) + 4 * sizeof(uint64_t)) +
+               (size_t)G * 2 * (2 * sizeof(float4) + sizeof(float2)) + 64;
     }
-    static size_t smem_bytes(int R, int slot_floats) {
-        return (size_t)R * slot_floats * sizeof(float) + ctrl_bytes(R);
+    static size_t smem_bytes(int R, int slot_floats, int G) {
+        return (size_t)R * slot_floats * sizeof(float) + ctrl_bytes(R, G);
     }
     __device__ static Smem carve(const TArgs &a, unsigned char *raw) {
         Smem s;
@@ -151,20 +182,24 @@ struct Stage {
         o += (size_t)kTGroupRing * 2 * sizeof(double2);
         s.lcnt = reinterpret_cast<double *>(raw + o);
         o += (size_t)kTGroupRing * 2 * sizeof(double);
-        s.ctab = reinterpret_cast<float4 *>(raw + o);
-        o += (size_t)kTGroupRing * 2 * sizeof(float4);
-        s.stab = reinterpret_cast<float4 *>(raw + o);
-        o += (size_t)kTGroupRing * 2 * sizeof(float4);
         s.ptab = reinterpret_cast<float *>(raw + o);
         o += (size_t)kTGroupRing * 16 * sizeof(float);
-        s.stats_upto = reinterpret_cast<int *>(raw + o);
-        o += kTStats * sizeof(int);
-        s.apply_upto = reinterpret_cast<int *>(raw + o);
-        o += kTApply * sizeof(int);
-        s.ready_upto = reinterpret_cast<int *>(raw + o);
-        o += sizeof(int);
-        s.published = reinterpret_cast<int *>(raw + o);
-        o += sizeof(int);
+        s.ctab = reinterpret_cast<float4 *>(raw + o);
+        o += (size_t)a.G * 2 * sizeof(float4);
+        s.stab = reinterpret_cast<float4 *>(raw + o);
+        o += (size_t)a.G * 2 * sizeof(float4);
+        s.otab = reinterpret_cast<float2 *>(raw + o);
+        o += (size_t)a.G * 2 * sizeof(float2);
+        s.sbar = reinterpret_cast<uint64_t *>(raw + o);
+        o += kTGroupRing * sizeof(uint64_t);
+        s.pbar = reinterpret_cast<uint64_t *>(raw + o);
+        o += kTGroupRing * sizeof(uint64_t);
+        s.rbar = reinterpret_cast<uint64_t *>(raw + o);
+        o += kTGroupRing * sizeof(uint64_t);
+        s.abar = reinterpret_cast<uint64_t *>(raw + o);
+        o += kTGroupRing * sizeof(uint64_t);
+        s.tbar = reinterpret_cast<uint64_t *>(raw + o);
+        o += sizeof(uint64_t);
         s.stop = reinterpret_cast<int *>(raw + o);
         return s;
     }
@@ -192,44 +227,18 @@ struct Stage {
                 }
             }
             if (__shfl_sync(0xffffffffu, quit, 0)) return false;
+            __nanosleep(64);
         }
     }
-    // whole warp, warp-uniform result: until min(counters[0..n)) >= want
-    __device__ static bool wait_min(const TArgs &a, const Smem &s, const int *counters, int n, int want) {
-        const unsigned long long deadline = global_ns() + a.wait_ns;
-        for (;;) {
-            int ok = 0, quit = 0;
-            if ((threadIdx.x & 31) == 0) {
-                int m = 0x7fffffff;
-                for (int i = 0; i < n; ++i) {
-                    const int v = reinterpret_cast<const volatile int *>(counters)[i];
-                    m = v < m ? v : m;
-                }
-                ok = m >= want;
-                if (!ok) {
-                    if (stopped(s)) {
-                        quit = 1;
-                    } else if (global_ns() > deadline) {
-                        give_up(a, s, DEVERR_WAIT_BARRIER);
-                        quit = 1;
-                    }
-                }
-            }
-            if (__shfl_sync(0xffffffffu, ok, 0)) {
-                __threadfence_block();
-                return true;
-            }
-            if (__shfl_sync(0xffffffffu, quit, 0)) return false;
-            __nanosleep(32);
-        }
+    // whole warp: wait for group g's phase of the group barrier array `bars`
+    __device__ static bool wait_group(const TArgs &a, const Smem &s, uint64_t *bars, int g) {
+        return wait_bar(a, s, &bars[g % kTGroupRing], (unsigned)(g / kTGroupRing) & 1u);
     }
-    // lane 0 of a warp: publish a progress counter after the warp's shared-memory writes
-    __device__ static void post(int *counter, int value) {
+    // whole warp: lane 0 arrives on group g's barrier of `bars` after the warp's
+    // shared-memory writes (the arrive releases them to the waiters)
+    __device__ static void arrive_group(uint64_t *bars, int g) {
         __syncwarp();
-        if ((threadIdx.x & 31) == 0) {
-            __threadfence_block();
-            *reinterpret_cast<volatile int *>(counter) = value;
-        }
+        if ((threadIdx.x & 31) == 0) mbar_arrive(&bars[g % kTGroupRing]);
         __syncwarp();
     }
 
@@ -242,40 +251,86 @@ struct Stage {
         return ((n * (uint32_t)a.C + c) * (uint32_t)a.S) + k * (uint32_t)a.U;
     }
 
+    // ---- prologue (every warp but the producer) ----
+    // The per-channel inputs of every group's share channels into the tables, all loads in
+    // flight at once; each warp's lane 0 then arrives on tbar.
+    __device__ static void load_tables(const TArgs &a, const Smem &s, int rid) {
+        const int t = (int)threadIdx.x - 32, nt = kTThreads - 32;
+        for (int i = t; i < 2 * a.G; i += nt) {
+            const int g = i >> 1, j = i & 1;
+            const Share sh = share_of(a, g, rid, a.f_ps);
+            if (j >= sh.nseg) continue;
+            const int cl = sh.cfirst + j;
+            const int64_t c = (int64_t)sh.c0 + cl;
+            // the accumulated outputs are read only by the CTA that writes them
+            const bool owner = owner_of(a, g, (uint32_t)cl * a.NK, a.Ps) == rid;
+            if (BWD) {
+                const float m = a.io.mean_in[c], v = a.io.var_in[c], gm = a.io.scales[c], bt = a.io.biases[c];
+                s.ctab[i] = make_float4(m, v, gm, bt);
+                // the forward's normalisation (batchnorm.zig:142), to recompute y from x
+                s.stab[i] = make_float4(m, 1.0f / (sqrtf(v) + 0.000001f), gm, bt);
+                if (owner) s.otab[i] = make_float2(a.io.bias_upd[c], a.io.scale_upd[c]);
+            } else {
+                s.ctab[i] = make_float4(a.io.scales[c], a.io.biases[c], 0.0f, 0.0f);
+                if (owner) s.otab[i] = make_float2(a.io.rmean[c], a.io.rvar[c]);
+            }
+        }
+        __syncwarp();
+        if ((threadIdx.x & 31) == 0) mbar_arrive(s.tbar);
+        __syncwarp();
+    }
+
     // ---- producer warp ----
     // Units are numbered in the CTA's order of groups and units; unit i lives in slot i % R
-    // and is that slot's (i / R)-th occupant.
+    // and is that slot's (i / R)-th occupant. The warp issues up to min(32, R) units at once,
+    // one per lane: a unit waits for the slot of unit i - R, which belongs to a group at least
+    // two groups back (a group's share is at most R / 2 units), so no unit of a batch waits
+    // for another unit of the same or a later batch.
     __device__ static void producer(const TArgs &a, const Smem &s, int rid) {
         const int lane = threadIdx.x & 31;
         const uint64_t pol = l2_evict_first();
-        uint32_t i = 0;  // units issued
+        const uint32_t width = a.R < 32 ? (uint32_t)a.R : 32u;
+        uint32_t i0 = 0;      // the CTA's unit number of the current group's first unit
+        uint32_t issued = 0;  // units whose copies have been issued (in unit order)
         bool ok = true;
         for (int g = 0; g < a.G && ok; ++g) {
-            // group g reuses the state buffer of group g - kTGroupRing: wait until that
-            // group's outputs are written
-            if (g >= kTGroupRing && !wait_min(a, s, s.apply_upto, kTApply, g - kTGroupRing + 1)) {
+            // group g reuses the state buffer of group g - kTGroupRing: wait until every output
+            // warp is done with that group
+            if (g >= kTGroupRing && !wait_group(a, s, s.abar, g - kTGroupRing)) {
                 ok = false;
                 break;
             }
             const Share sh = share_of(a, g, rid, a.f_ps);
-            const int b = g % kTGroupRing;
-            if (BWD && lane < sh.nseg) {
-                // the forward's normalisation of the share's channels (batchnorm.zig:142), for
-                // the statistics warps' recomputation of y; visible to them through the
-                // release of the unit barriers below
-                const int64_t c = (int64_t)sh.c0 + sh.cfirst + lane;
-                const float m = a.io.mean_in[c], v = a.io.var_in[c];
-                s.stab[2 * b + lane] = make_float4(m, 1.0f / (sqrtf(v) + 0.000001f), a.io.scales[c], a.io.biases[c]);
-            }
-            __syncwarp();
             const uint32_t n_units = sh.t1 - sh.t0;
-            for (uint32_t u = 0; u < n_units; ++u, ++i) {
-                const uint32_t slot = i % (uint32_t)a.R, use = i / (uint32_t)a.R;
-                if (use > 0 && !wait_bar(a, s, &s.empty[slot], (use - 1) & 1u)) {
-                    ok = false;
-                    break;
+            for (uint32_t base = 0; base < n_units && ok; base += width) {
+                const uint32_t u = base + (uint32_t)lane;
+                const bool has = (uint32_t)lane < width && u < n_units;
+                const uint32_t i = i0 + u, slot = i % (uint32_t)a.R, use = i / (uint32_t)a.R;
+                // every lane's slot free (its previous occupant written out)
+                bool free_ = !has || use == 0 || mbar_test(&s.empty[slot], (use - 1) & 1u);
+                if (!__all_sync(0xffffffffu, free_)) {
+                    const unsigned long long deadline = global_ns() + a.wait_ns;
+                    for (;;) {
+                        free_ = free_ || mbar_test(&s.empty[slot], (use - 1) & 1u);
+                        if (__all_sync(0xffffffffu, free_)) break;
+                        int quit = 0;
+                        if (lane == 0) {
+                            if (stopped(s)) {
+                                quit = 1;
+                            } else if (global_ns() > deadline) {
+                                give_up(a, s, DEVERR_WAIT_BARRIER);
+                                quit = 1;
+                            }
+                        }
+                        if (__shfl_sync(0xffffffffu, quit, 0)) {
+                            ok = false;
+                            break;
+                        }
+                        __nanosleep(64);
+                    }
+                    if (!ok) break;  // no unit of this batch was issued
                 }
-                if (lane == 0) {
+                if (has) {
                     const uint32_t off = unit_offset(a, g, sh.t0 + u);
                     // vec: the unit is 16-byte aligned; otherwise copy the aligned span around it
                     const uint32_t start = a.vec ? off : (off & ~3u);
@@ -287,29 +342,53 @@ struct Stage {
                     if (NT > 2) bulk_load(dst + 2 * a.SU, a.io.t2 + start, len * 4, &s.full[slot], pol);
                 }
                 __syncwarp();
+                issued = i0 + (base + width < n_units ? base + width : n_units);
+            }
+            i0 += n_units;
+            // Bring the share of group g + 2 into L2 now: its loads are issued only once
+            // slots come free, and then come from L2 while HBM streams the groups after it.
+            // Groups that fit the ring at the start are loaded at once and need no prefetch.
+            const int q = g + 2;
+            if (ok && q < a.G && q >= a.pf_from) {
+                const Share sq = share_of(a, q, rid, a.f_ps);
+                for (uint32_t u = lane; u < sq.t1 - sq.t0; u += 32) {
+                    const uint32_t off = unit_offset(a, q, sq.t0 + u);
+                    const uint32_t start = a.vec ? off : (off & ~3u);
+                    const uint32_t len = a.vec ? (uint32_t)a.U : ((off - start + (uint32_t)a.U + 3u) & ~3u);
+                    prefetch_l2(a.io.t0 + start, len * 4);
+                    if (NT > 1) prefetch_l2(a.io.t1 + start, len * 4);
+                    if (NT > 2) prefetch_l2(a.io.t2 + start, len * 4);
+                }
+                __syncwarp();
             }
         }
-        // before the CTA may exit, every copy issued into its shared memory must have landed:
-        // the current occupants of the slots, the last R units issued (older ones have been
-        // consumed). On the normal path they have landed or are about to.
-        const uint32_t first = i > (uint32_t)a.R ? i - (uint32_t)a.R : 0u;
+        drain(a, s, issued);
+    }
+
+    // Before the CTA may exit, every copy issued into its shared memory must have landed: the
+    // current occupants of the slots, i.e. the last R units issued (older ones have been
+    // consumed). On the normal path they have landed already or are about to.
+    __device__ static void drain(const TArgs &a, const Smem &s, uint32_t issued) {
+        const uint32_t first = issued > (uint32_t)a.R ? issued - (uint32_t)a.R : 0u;
         const unsigned long long deadline = global_ns() + a.wait_ns;
-        for (uint32_t k = first; k < i; ++k) {
+        for (uint32_t k = first + (threadIdx.x & 31); k < issued; k += 32) {
             const uint32_t slot = k % (uint32_t)a.R;
             while (!mbar_test(&s.full[slot], (k / (uint32_t)a.R) & 1u) && global_ns() < deadline) {
+                __nanosleep(64);
             }
         }
-        (void)ok;
+        __syncwarp();
     }
 
     // ---- statistics warps ----
     __device__ static void stats(const TArgs &a, const Smem &s, int rid, int ws) {
         const int lane = threadIdx.x & 31;
+        if (BWD && !wait_bar(a, s, s.tbar, 0)) return;  // the forward's parameters (stab)
         uint32_t i0 = 0;  // the CTA's unit number of the group's first unit
         for (int g = 0; g < a.G; ++g) {
             // a warp without units in the groups ahead would otherwise reach group g while the
             // publisher still reads group g - kTGroupRing's partials from the same buffer
-            if (g >= kTGroupRing && !wait_min(a, s, s.published, 1, g - kTGroupRing + 1)) return;
+            if (g >= kTGroupRing && !wait_group(a, s, s.pbar, g - kTGroupRing)) return;
             const Share sh = share_of(a, g, rid, a.f_ps);
             const int b = g % kTGroupRing;
             const uint32_t n_units = sh.t1 - sh.t0;
@@ -353,7 +432,7 @@ struct Stage {
                         s1 = s2 = 0.0f;
                         seg = useg;
                     }
-                    const float4 fp = s.stab[2 * b + seg];
+                    const float4 fp = s.stab[2 * g + seg];
                     BwdParam p;
                     p.m = fp.x;
                     p.inv = fp.y;
@@ -396,7 +475,7 @@ struct Stage {
                 s.wrec[(2 * b + 0) * kTStats + ws] = rec[0];
                 s.wrec[(2 * b + 1) * kTStats + ws] = rec[1];
             }
-            post(&s.stats_upto[ws], g + 1);
+            arrive_group(s.sbar, g);
             i0 += n_units;
         }
     }
@@ -410,7 +489,7 @@ struct Stage {
     __device__ static void publisher(const TArgs &a, const Smem &s, int rid, unsigned tag) {
         const int lane = threadIdx.x & 31;
         for (int g = 0; g < a.G; ++g) {
-            if (!wait_min(a, s, s.stats_upto, kTStats, g + 1)) return;
+            if (!wait_group(a, s, s.sbar, g)) return;
             const Share sh = share_of(a, g, rid, a.f_ps);
             const int b = g % kTGroupRing;
             for (int j = 0; j < sh.nseg; ++j) {
@@ -441,7 +520,7 @@ struct Stage {
                     st_record<kRecWords>(a.rec + (((size_t)g * a.Ps + rid) * 2 + j) * 4, q, tag, false);
                 }
             }
-            post(s.published, g + 1);
+            arrive_group(s.pbar, g);
         }
     }
 
@@ -505,7 +584,7 @@ struct Stage {
                         }
                     }
                     if (__shfl_sync(0xffffffffu, quit, 0)) return false;
-                    __nanosleep(20);
+                    __nanosleep(64);
                 }
             }
             double2 mine;
@@ -565,16 +644,10 @@ struct Stage {
 
     __device__ static void merger(const TArgs &a, const Smem &s, int rid, unsigned tag) {
         const int lane = threadIdx.x & 31;
+        if (!wait_bar(a, s, s.tbar, 0)) return;
         for (int g = 0; g < a.G; ++g) {
             const Share sh = share_of(a, g, rid, a.f_ps);
             const int b = g % kTGroupRing;
-            // the closing's per-channel inputs, loaded before the records are polled
-            if (lane < sh.nseg) {
-                const int64_t c = (int64_t)sh.c0 + sh.cfirst + lane;
-                s.ctab[2 * b + lane] = BWD ? make_float4(a.io.mean_in[c], a.io.var_in[c], a.io.scales[c], a.io.biases[c])
-                                           : make_float4(a.io.scales[c], a.io.biases[c], 0.0f, 0.0f);
-            }
-            __syncwarp();
             if (!merge(a, s, g, rid, tag)) {
                 // another CTA (or rank) gave up, or this wait did: stop this CTA's warps too
                 if (lane == 0) *reinterpret_cast<volatile int *>(s.stop) = 1;
@@ -583,7 +656,7 @@ struct Stage {
             if (lane == 0)
                 for (int j = 0; j < sh.nseg; ++j) {
                     const double2 tot = s.lrec[2 * b + j];
-                    const float4 ci = s.ctab[2 * b + j];
+                    const float4 ci = s.ctab[2 * g + j];
                     float *out = s.ptab + (2 * b + j) * 8;
                     if constexpr (!BWD) {
                         const FwdClose f = fwd_close(tot.x, tot.y, s.lcnt[2 * b + j]);
@@ -592,7 +665,7 @@ struct Stage {
                         *reinterpret_cast<BwdParam *>(out) = bwd_params(tot.x, tot.y, ci.x, ci.y, ci.z, ci.w, a.denom);
                     }
                 }
-            post(s.ready_upto, g + 1);
+            arrive_group(s.rbar, g);
             // the per-channel outputs, by the CTA that owns the channel's first unit
             if (lane == 0)
                 for (int j = 0; j < sh.nseg; ++j) {
@@ -600,19 +673,22 @@ struct Stage {
                     const int64_t c = (int64_t)sh.c0 + cl;
                     if (owner_of(a, g, (uint32_t)cl * a.NK, a.Ps) != rid) continue;
                     const double2 tot = s.lrec[2 * b + j];
+                    const float2 prior = s.otab[2 * g + j];  // read in the prologue; this CTA alone writes c
                     if constexpr (!BWD) {
                         const FwdClose f = fwd_close(tot.x, tot.y, s.lcnt[2 * b + j]);
-                        const float rm = a.io.rmean[c], rv = a.io.rvar[c];
                         a.io.mean[c] = f.m;
                         a.io.var[c] = f.var;
-                        a.io.rmean[c] = rolling(rm, f.m);
-                        a.io.rvar[c] = rolling(rv, f.var);
+                        a.io.rmean[c] = rolling(prior.x, f.m);
+                        a.io.rvar[c] = rolling(prior.y, f.var);
                     } else {
-                        const float4 ci = s.ctab[2 * b + j];
+                        const float4 ci = s.ctab[2 * g + j];
                         float md;
                         const BwdParam p = bwd_params(tot.x, tot.y, ci.x, ci.y, ci.z, ci.w, a.denom, &md);
-                        bwd_write(tot.x, tot.y, p, md, a.io.bias_upd, a.io.scale_upd, a.io.mean_delta, a.io.var_delta,
-                                  c);
+                        // bwd_write's accumulation, on the prior values
+                        a.io.bias_upd[c] = prior.x + (float)tot.x;
+                        a.io.scale_upd[c] = prior.y + (float)(tot.y * (double)p.inv);
+                        a.io.mean_delta[c] = md;
+                        a.io.var_delta[c] = p.vd;
                     }
                 }
             __syncwarp();
@@ -620,25 +696,46 @@ struct Stage {
     }
 
     // ---- output warps ----
+    // With a.bulk_out the outputs are written over the unit's first tensor in its slot and
+    // leave by one bulk copy per unit (lane 0's bulk groups, one per unit); the slot returns
+    // to the producer once that copy has read it, which lane 0 checks one unit later (or at
+    // the group's end, so that no slot stays held while the warp waits for the next group).
+    // Otherwise the lanes store the outputs themselves and the slot returns at once.
     __device__ static void apply(const TArgs &a, const Smem &s, int rid, int wa) {
         const int lane = threadIdx.x & 31;
         uint32_t i0 = 0;
+        int held = -1;  // lane 0: the slot whose bulk copy may still read it
         for (int g = 0; g < a.G; ++g) {
             const Share sh = share_of(a, g, rid, a.f_ps);
             const int b = g % kTGroupRing;
             const uint32_t n_units = sh.t1 - sh.t0;
-            if (n_units > (uint32_t)wa && !wait_min(a, s, s.ready_upto, 1, g + 1)) return;
+            if (n_units > (uint32_t)wa && !wait_group(a, s, s.rbar, g)) break;
+            bool ok = true;
             for (uint32_t u = wa; u < n_units; u += kTApply) {
                 const uint32_t i = i0 + u, slot = i % (uint32_t)a.R;
                 // already complete (the statistics waited on it): the acquire of its data
-                if (!wait_bar(a, s, &s.full[slot], (i / (uint32_t)a.R) & 1u)) return;
+                if (!wait_bar(a, s, &s.full[slot], (i / (uint32_t)a.R) & 1u)) {
+                    ok = false;
+                    break;
+                }
                 const int seg = sh.t0 + u >= sh.bnd ? 1 : 0;
                 const float *pt = s.ptab + (2 * b + seg) * 8;
                 const uint32_t off = unit_offset(a, g, sh.t0 + u);
-                const float *src = s.ring + (size_t)slot * a.slot_floats;
+                float *src = s.ring + (size_t)slot * a.slot_floats;
                 if constexpr (!BWD) {
                     const float4 p = *reinterpret_cast<const float4 *>(pt);
-                    if (a.vec) {
+                    if (a.bulk_out) {
+                        float4 *v4 = reinterpret_cast<float4 *>(src);
+                        const int n4 = a.U >> 2;
+#pragma unroll 4
+                        for (int k = lane; k < n4; k += 32) {
+                            const float4 v = v4[k];
+                            v4[k] = make_float4(bn_fwd1<A>(v.x, p.x, p.y, p.z, p.w, a.act),
+                                                bn_fwd1<A>(v.y, p.x, p.y, p.z, p.w, a.act),
+                                                bn_fwd1<A>(v.z, p.x, p.y, p.z, p.w, a.act),
+                                                bn_fwd1<A>(v.w, p.x, p.y, p.z, p.w, a.act));
+                        }
+                    } else if (a.vec) {
                         const float4 *v4 = reinterpret_cast<const float4 *>(src);
                         const int n4 = a.U >> 2;
                         float *dst = a.io.out + off;
@@ -664,7 +761,7 @@ struct Stage {
                 } else {
                     const BwdParam p = *reinterpret_cast<const BwdParam *>(pt);
                     if (a.vec) {
-                        const float4 *d4 = reinterpret_cast<const float4 *>(src);
+                        float4 *d4 = reinterpret_cast<float4 *>(src);
                         const float4 *x4 = reinterpret_cast<const float4 *>(src + a.SU);
                         const float4 *y4 = reinterpret_cast<const float4 *>(src + 2 * a.SU);
                         const int n4 = a.U >> 2;
@@ -673,11 +770,15 @@ struct Stage {
                         for (int k = lane; k < n4; k += 32) {
                             const float4 d = d4[k], xv = x4[k];
                             const float4 yy = HASY ? y4[k] : xv;
-                            st4(dst + 4 * k,
+                            const float4 r =
                                 make_float4(bn_dx_p(bn_grad1<A, HASY>(d.x, xv.x, yy.x, p, a.act), xv.x, p, a),
                                             bn_dx_p(bn_grad1<A, HASY>(d.y, xv.y, yy.y, p, a.act), xv.y, p, a),
                                             bn_dx_p(bn_grad1<A, HASY>(d.z, xv.z, yy.z, p, a.act), xv.z, p, a),
-                                            bn_dx_p(bn_grad1<A, HASY>(d.w, xv.w, yy.w, p, a.act), xv.w, p, a)));
+                                            bn_dx_p(bn_grad1<A, HASY>(d.w, xv.w, yy.w, p, a.act), xv.w, p, a));
+                            if (a.bulk_out)
+                                d4[k] = r;  // over delta, element by element
+                            else
+                                st4(dst + 4 * k, r);
                         }
                     } else {
                         const uint32_t o = off & 3u;
@@ -689,13 +790,39 @@ struct Stage {
                         }
                     }
                 }
-                // the unit's slot is read: hand it back to the producer
+                if (a.bulk_out) {
+                    fence_proxy_async();  // the lanes' shared-memory writes, before the bulk copy reads them
+                    __syncwarp();
+                    if (lane == 0) {
+                        bulk_store(a.io.out + off, src, (unsigned)a.U * 4u);
+                        bulk_commit();
+                        if (held >= 0) {
+                            bulk_wait_read<1>();  // the previous unit's copy has read its slot
+                            mbar_arrive(&s.empty[held]);
+                        }
+                        held = (int)slot;
+                    }
+                } else {
+                    // the unit's slot is read: hand it back to the producer
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&s.empty[slot]);
+                }
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&s.empty[slot]);
             }
-            post(&s.apply_upto[wa], g + 1);
+            if (lane == 0 && held >= 0) {
+                bulk_wait_read<0>();
+                mbar_arrive(&s.empty[held]);
+                held = -1;
+            }
+            __syncwarp();
+            if (!ok) break;
+            arrive_group(s.abar, g);
             i0 += n_units;
         }
+        // every bulk copy of this warp complete (read from the slots and written out) before
+        // the CTA may end
+        if (lane == 0) bulk_wait_all();
+        __syncwarp();
     }
 };
 
@@ -710,12 +837,15 @@ __global__ void __launch_bounds__(kTThreads, 1) k_bn_stage(TArgs a) {
     if (threadIdx.x == 0) {
         s_epoch = ld_volatile(&a.sync[0]);
         *s.stop = 0;
-        *s.ready_upto = 0;
-        *s.published = 0;
         s_exited = 0;
     }
-    if (threadIdx.x < kTStats) s.stats_upto[threadIdx.x] = 0;
-    if (threadIdx.x < kTApply) s.apply_upto[threadIdx.x] = 0;
+    if (threadIdx.x == 0) mbar_init(s.tbar, kTWarps - 1);
+    if (threadIdx.x < kTGroupRing) {
+        mbar_init(&s.sbar[threadIdx.x], kTStats);
+        mbar_init(&s.pbar[threadIdx.x], 1);
+        mbar_init(&s.rbar[threadIdx.x], 1);
+        mbar_init(&s.abar[threadIdx.x], kTApply);
+    }
     for (int i = threadIdx.x; i < a.R; i += kTThreads) {
         mbar_init(&s.full[i], 1);
         mbar_init(&s.empty[i], 1);
@@ -729,6 +859,7 @@ __global__ void __launch_bounds__(kTThreads, 1) k_bn_stage(TArgs a) {
     // finish does it); in the launch whose successor's tag would wrap to 0, the last warp of
     // the last CTA clears the record area instead (once per 2^32 - 1 launches)
     const bool wraps = epoch + 2u == 0u;
+    if (warp != 0) K::load_tables(a, s, rid);
     if (warp == 0) {
         K::producer(a, s, rid);
     } else if (warp < kTWarpApply0) {
@@ -760,7 +891,7 @@ __global__ void __launch_bounds__(kTThreads, 1) k_bn_stage(TArgs a) {
 
 struct TPlan {
     bool ok = false;
-    int K = 0, U = 0, SU = 0, cg = 0, G = 0, cap = 0, R = 0, vec = 0;
+    int K = 0, U = 0, SU = 0, cg = 0, G = 0, cap = 0, R = 0, vec = 0, pf_from = 0;
     size_t smem = 0;
 };
 
@@ -801,12 +932,27 @@ TPlan plan_stage(int64_t batch, int64_t filters, int64_t spatial, int P, size_t 
     const size_t slot_bytes = (size_t)nt * pl.SU * sizeof(float);
     int R = 0;
     for (int r = kTMaxSlots; r >= 2; --r)
-        if (KS::smem_bytes(r, nt * pl.SU) <= smem_avail) {
+        if (KS::smem_bytes(r, nt * pl.SU, kMaxSweepGroups) <= smem_avail) {
             R = r;
             break;
         }
     if (R < 2 || slot_bytes * 2 > smem_avail) return pl;
     const int64_t NK = batch * pl.K;
+    // a tensor whose shares all fit the ring at once is one group: one exchange in all
+    {
+        const int64_t T = filters * NK;
+        const int64_t cap = (T + P - 1) / P;
+        if (filters <= P && cap <= R && (uint64_t)T * (uint64_t)P < (1ull << 32) - (uint64_t)P) {
+            pl.cg = (int)filters;
+            pl.G = 1;
+            pl.cap = (int)cap;
+            pl.R = R;
+            pl.smem = KS::smem_bytes(R, nt * pl.SU, 1);
+            pl.pf_from = 1;
+            pl.ok = true;
+            return pl;
+        }
+    }
     for (int D = 3; D >= 2 && !pl.ok; --D) {
         const int64_t capmax = R / D;
         if (capmax < 1) continue;
@@ -824,7 +970,8 @@ TPlan plan_stage(int64_t batch, int64_t filters, int64_t spatial, int P, size_t 
         pl.G = (int)G;
         pl.cap = (int)((T + P - 1) / P);
         pl.R = R;
-        pl.smem = KS::smem_bytes(R, nt * pl.SU);
+        pl.smem = KS::smem_bytes(R, nt * pl.SU, pl.G);
+        pl.pf_from = pl.cap > 0 ? R / pl.cap : pl.G;
         pl.ok = true;
     }
     return pl;
@@ -843,10 +990,11 @@ dnb_status run_stage(int64_t batch, int64_t filters, int64_t spatial, int act, c
     *launched = false;
     DeviceState *ds = nullptr;
     DNB_TRY(current_device(&ds));
-    // every tensor the copies read starts 16-byte aligned
+    // every tensor the bulk copies and the vector stores touch starts 16-byte aligned
     const void *ins[3] = {io.t0, io.t1, io.t2};
     for (int k = 0; k < (BWD ? (HASY ? 3 : 2) : 1); ++k)
         if (!aligned16(ins[k])) return DNB_OK;
+    if (!aligned16(io.out) || (io.xnorm && !aligned16(io.xnorm))) return DNB_OK;
     const int P = ds->sm_count;
     // dynamic shared memory: what a CTA may opt into, less room for the kernel's own static
     // variables
@@ -892,6 +1040,8 @@ dnb_status run_stage(int64_t batch, int64_t filters, int64_t spatial, int act, c
         a.SU = pl.SU;
         a.slot_floats = (BWD ? (HASY ? 3 : 2) : 1) * pl.SU;
         a.vec = pl.vec;
+        a.pf_from = pl.pf_from;
+        a.bulk_out = pl.vec && io.xnorm == nullptr;
         a.io = io;
         a.act = act;
         a.rec = ws->recs;
