@@ -41,10 +41,16 @@ SHAPES = [
 FULL_SHAPES = [(128, 128, 1024), (128, 256, 784), (64, 128, 1024)]
 
 
-# The fused entries pick a persistent kernel (the L2 sweep, else the shared-memory-staged
-# kernel), else the generic multi-launch path; the library reads these switches at every
-# call, so each test below runs each path on the same inputs.
-BN_PATHS = {"stage": {"DNB_BN_SWEEP": "0"}, "sweep": {"DNB_BN_STAGE": "0"}, "generic": {"DNB_BN_PERSISTENT": "0"}}
+# The fused entries pick a persistent kernel (the cluster-per-channel kernel, else the L2
+# sweep, else the grid-wide shared-memory-staged kernel), else the generic multi-launch path;
+# the library reads these switches at every call, so each test below runs each path on the
+# same inputs.
+BN_PATHS = {
+    "cluster": {},
+    "sweep": {"DNB_BN_CLUSTER": "0", "DNB_BN_STAGE": "0"},
+    "stage": {"DNB_BN_CLUSTER": "0", "DNB_BN_SWEEP": "0"},
+    "generic": {"DNB_BN_PERSISTENT": "0"},
+}
 
 
 @pytest.fixture(params=list(BN_PATHS))
