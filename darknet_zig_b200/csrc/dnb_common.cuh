@@ -54,7 +54,8 @@ struct DeviceState {
 // Scratch owned by the library for one (device, stream) pair.
 struct Workspace {
     cudaStream_t stream = nullptr;
-    // persistent-kernel state: [0] = launch epoch, [1] = CTAs that finished the current launch
+    // persistent-kernel state: [0] = launch epoch, [1] = CTAs that finished the current launch;
+    // [2] = blocks of the fused softmax + cross entropy that have left their row losses
     unsigned *sync = nullptr;
     size_t sync_words = 0;
     void *scratch = nullptr;  // per-channel partials of the multi-launch paths
@@ -64,7 +65,8 @@ struct Workspace {
     size_t rec_words = 0;
 };
 
-constexpr size_t kSyncWords = 2;
+constexpr size_t kSyncWords = 3;
+constexpr size_t kSyncSoftmaxDone = 2;
 
 // A sync-BN communicator as a kernel sees it (dnb_comm.cu): this rank, the ranks, and every
 // rank's exchange buffer of tagged records, 64-bit words

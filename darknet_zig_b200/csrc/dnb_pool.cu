@@ -3,6 +3,8 @@
 // (pooling.zig:146-158, darknet_kernels.hip:541-549).
 #include <float.h>
 
+#include <atomic>
+
 #include "dnb_common.cuh"
 
 namespace dnb {
@@ -103,6 +105,32 @@ __global__ void __launch_bounds__(kThreads) k_maxpool_2x2(int64_t pairs, int in_
     }
 }
 
+// The same 2x2 / stride-2 window on images whose width is even but not a multiple of 4
+// (14 x 14 at BASELINE config 2): one thread per output reads one 8-byte pair of each of
+// its two input rows; the comparisons and their order are k_maxpool_2x2's.
+__global__ void __launch_bounds__(kThreads) k_maxpool_2x2_pair(int64_t out_n, int in_w, FastDiv fow, FastDiv foh,
+                                                               const float *__restrict__ in, float *__restrict__ out,
+                                                               int32_t *__restrict__ idx) {
+    const int64_t step = (int64_t)gridDim.x * kThreads;
+    for (int64_t id = (int64_t)blockIdx.x * kThreads + threadIdx.x; id < out_n; id += step) {
+        uint32_t t, j, q, i;
+        fow.divmod((uint32_t)id, t, j);
+        foh.divmod(t, q, i);
+        const int64_t row0 = ((int64_t)q * (2 * foh.d) + 2 * i) * in_w + 2 * (int64_t)j;
+        const int64_t row1 = row0 + in_w;
+        const float2 a = *reinterpret_cast<const float2 *>(in + row0);
+        const float2 b = *reinterpret_cast<const float2 *>(in + row1);
+        float v = -FLT_MAX;
+        int k = -1;
+        if (a.x > v) { v = a.x; k = (int)row0; }
+        if (a.y > v) { v = a.y; k = (int)row0 + 1; }
+        if (b.x > v) { v = b.x; k = (int)row1; }
+        if (b.y > v) { v = b.y; k = (int)row1 + 1; }
+        out[id] = v;
+        idx[id] = k;
+    }
+}
+
 __device__ __forceinline__ int ceil_div_pos(int a, int b) { return a >= 0 ? (a + b - 1) / b : a / b; }
 
 // pooling.zig:95-103 as a gather: input element `in` receives, in increasing output index,
@@ -135,10 +163,12 @@ __global__ void __launch_bounds__(kThreads) k_maxpool_bwd(int64_t in_n, int in_h
     }
 }
 
-// pooling.zig:146-158. A block stages PB consecutive planes (PB*S floats, contiguous) in
-// shared memory with coalesced 128-bit loads; thread t then sums plane t in order, exactly
-// as the CPU loop does, so the output is bit-identical. The planes are read once.
-__global__ void __launch_bounds__(kThreads) k_avgpool_fwd(int64_t planes, int S, int PB, bool vec,
+// pooling.zig:146-158. A block of kAvgThreads threads stages PB consecutive planes (PB*S
+// floats, contiguous) in shared memory with coalesced 128-bit loads; thread t then sums
+// plane t in order, exactly as the CPU loop does, so the output is bit-identical. The planes
+// are read once. Small blocks with small tiles let an SM keep many tiles in flight.
+constexpr int kAvgThreads = 64;
+__global__ void __launch_bounds__(kAvgThreads) k_avgpool_fwd(int64_t planes, int S, int PB, bool vec,
                                                           const float *__restrict__ in, float *__restrict__ out) {
     extern __shared__ __align__(16) float tile[];
     const float denom = (float)S;
@@ -150,13 +180,13 @@ __global__ void __launch_bounds__(kThreads) k_avgpool_fwd(int64_t planes, int S,
         if (vec) {
             const int nf4 = nf >> 2;
             const float4 *src = reinterpret_cast<const float4 *>(in + base);
-            for (int k = threadIdx.x; k < nf4; k += kThreads) reinterpret_cast<float4 *>(tile)[k] = __ldcs(src + k);
-            for (int k = (nf4 << 2) + threadIdx.x; k < nf; k += kThreads) tile[k] = in[base + k];
+            for (int k = threadIdx.x; k < nf4; k += kAvgThreads) reinterpret_cast<float4 *>(tile)[k] = __ldcs(src + k);
+            for (int k = (nf4 << 2) + threadIdx.x; k < nf; k += kAvgThreads) tile[k] = in[base + k];
         } else {
-            for (int k = threadIdx.x; k < nf; k += kThreads) tile[k] = in[base + k];
+            for (int k = threadIdx.x; k < nf; k += kAvgThreads) tile[k] = in[base + k];
         }
         __syncthreads();
-        for (int t = threadIdx.x; t < np; t += kThreads) {
+        for (int t = threadIdx.x; t < np; t += kAvgThreads) {
             const float *row = tile + (int64_t)t * S;
             float sum = 0.0f;
             for (int s = 0; s < S; ++s) sum += row[s];
@@ -210,6 +240,10 @@ dnb_status dnb_forward_maxpool(int64_t out_n, int64_t in_h, int64_t in_w, int64_
         k_maxpool_2x2<<<grid_for(pairs, kThreads, ds), kThreads, 0, s>>>(
             pairs, (int)in_w, (int)out_w, FastDiv((uint32_t)(out_w / 2)), FastDiv((uint32_t)out_h), input, output,
             indexes);
+    } else if (size == 2 && stride == 2 && off == 0 && in_h == 2 * out_h && in_w == 2 * out_w && fast &&
+               (reinterpret_cast<uintptr_t>(input) & 7u) == 0) {
+        k_maxpool_2x2_pair<<<grid, kThreads, 0, s>>>(out_n, (int)in_w, FastDiv((uint32_t)out_w),
+                                                     FastDiv((uint32_t)out_h), input, output, indexes);
     } else if (size == 2)
         k_maxpool_fwd<2><<<grid, kThreads, 0, s>>>(out_n, (int)in_h, (int)in_w, (int)out_h, (int)out_w, (int)stride, 2,
                                                    off, fw, fh, fast, input, output, indexes);
@@ -250,18 +284,26 @@ dnb_status dnb_forward_avgpool(int64_t n, int64_t w, int64_t h, int64_t c, const
     DNB_TRY(current_device(&ds));
     const cudaStream_t s = as_stream(stream);
     const int64_t S = w * h;
-    // planes per block: a multiple of 4 (so a tile starts 16-byte aligned) with the tile
-    // within 96 KB of shared memory
-    int64_t pb = (96 * 1024) / (S * 4);
-    if (pb > kThreads) pb = kThreads;
+    // planes per block: a multiple of 4 (so a tile starts 16-byte aligned), at most one per
+    // thread, with the tile within 16 KB of shared memory (96 KB for planes of more than 256
+    // floats, so that a block still sums at least 4 planes in the CPU's order)
+    const int64_t budget = S <= 256 ? 16 * 1024 : 96 * 1024;
+    int64_t pb = budget / (S * 4);
+    if (pb > kAvgThreads) pb = kAvgThreads;
     pb &= ~(int64_t)3;
-    if (pb >= 32) {
+    if (pb >= 4) {
         const size_t smem = (size_t)pb * S * sizeof(float);
-        if (smem > 48 * 1024)
-            DNB_CUDA(cudaFuncSetAttribute(k_avgpool_fwd, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        if (smem > 48 * 1024) {
+            static std::atomic<int> big[kMaxDevices];
+            if (!big[ds->device].load(std::memory_order_relaxed)) {
+                DNB_CUDA(cudaFuncSetAttribute(k_avgpool_fwd, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024));
+                big[ds->device].store(1, std::memory_order_relaxed);
+            }
+        }
         const int64_t blocks = (n + pb - 1) / pb;
-        const unsigned grid = (unsigned)(blocks < (int64_t)ds->sm_count * 4 ? blocks : (int64_t)ds->sm_count * 4);
-        k_avgpool_fwd<<<grid, kThreads, smem, s>>>(n, (int)S, (int)pb, aligned16(input), input, output);
+        const int64_t cap = (int64_t)ds->sm_count * 32;
+        const unsigned grid = (unsigned)(blocks < cap ? blocks : cap);
+        k_avgpool_fwd<<<grid, kAvgThreads, smem, s>>>(n, (int)S, (int)pb, aligned16(input), input, output);
     } else {
         k_avgpool_fwd_warp<<<grid_for(n * 32, kThreads, ds), kThreads, 0, s>>>(n, S, input, output);
     }

@@ -7,6 +7,8 @@
 // arithmetic is the CPU's (exp(x/temp - largest/temp), then e/sum); the sum is a tree.
 #include <float.h>
 
+#include <atomic>
+
 #include "dnb_common.cuh"
 
 namespace dnb {
@@ -113,11 +115,30 @@ __device__ __forceinline__ float block_sum_f(float v, float *red) {
     return t;
 }
 
+// With `cost`, the last block to finish (a counter in the stream's workspace, reset by that
+// block) adds the row losses in fp64 in row order -- the same sum k_cost forms -- so the
+// loss needs no second launch.
+__device__ __forceinline__ void cost_sum(const float *row_loss, int64_t batch, float *cost) {
+    __shared__ double part[32];
+    double s = 0.0;
+    for (int64_t i = threadIdx.x; i < batch; i += blockDim.x) s += (double)row_loss[i];
+    s = warp_sum(s);
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = s;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        double t = threadIdx.x < (blockDim.x >> 5) ? part[threadIdx.x] : 0.0;
+        t = warp_sum(t);
+        if (threadIdx.x == 0) *cost = (float)t;
+    }
+}
+
 __global__ void __launch_bounds__(kThreads) k_softmax_xent_rows(const float *in, const float *truth, int64_t n,
                                                                 int64_t batch, float temp, float *out, float *delta,
-                                                                float *err, float *row_loss) {
+                                                                float *err, float *row_loss, float *cost,
+                                                                unsigned *done) {
     extern __shared__ float row[];
     __shared__ float red[kWarps + 1];
+    __shared__ int s_last;
     for (int64_t q = blockIdx.x; q < batch; q += gridDim.x) {
         const int64_t off = q * n;
         float largest = -FLT_MAX;  // blas.zig:214
@@ -147,6 +168,15 @@ __global__ void __launch_bounds__(kThreads) k_softmax_xent_rows(const float *in,
         loss = block_sum_f(loss, red);
         if (threadIdx.x == 0 && row_loss) row_loss[q] = loss;
     }
+    if (!cost) return;
+    // this block's row losses, visible before it counts itself; the last block sums them all
+    __threadfence();
+    if (threadIdx.x == 0) s_last = atomicAdd(done, 1u) == gridDim.x - 1u;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    cost_sum(row_loss, batch, cost);
+    if (threadIdx.x == 0) *done = 0u;  // for the next launch on this stream
 }
 
 // The cost: rows added in fp64 in row order by one block (deterministic).
@@ -219,19 +249,31 @@ dnb_status dnb_softmax_xent(const float *input, const float *truth, int64_t n, i
         row_loss = static_cast<float *>(ws->scratch);
     }
     if (n <= kRowSmem) {
-        static size_t smem_set = 0;
+        // the per-device attribute for rows beyond the default 48 KB, set once to the most
+        // a staged row takes
         const size_t smem = sizeof(float) * (size_t)n;
-        if (smem > 48 * 1024 && smem > smem_set) {
-            DNB_CUDA(cudaFuncSetAttribute(k_softmax_xent_rows, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-            smem_set = smem;
+        if (smem > 48 * 1024) {
+            static std::atomic<int> big[kMaxDevices];
+            if (!big[ds->device].load(std::memory_order_relaxed)) {
+                DNB_CUDA(cudaFuncSetAttribute(k_softmax_xent_rows, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              (int)(sizeof(float) * kRowSmem)));
+                big[ds->device].store(1, std::memory_order_relaxed);
+            }
         }
         const int64_t cap = (int64_t)ds->sm_count * 8;
         const unsigned grid = (unsigned)(batch < cap ? batch : cap);
-        k_softmax_xent_rows<<<grid, kThreads, smem, s>>>(input, truth, n, batch, temp, output, delta, err, row_loss);
-    } else {
-        k_softmax_xent<<<rows_grid(batch, ds), kThreads, 0, s>>>(input, truth, n, batch, temp, output, delta, err,
-                                                                 row_loss);
+        Workspace *ws = nullptr;
+        unsigned *done = nullptr;
+        if (cost) {
+            DNB_TRY(workspace(s, sizeof(float) * (size_t)batch, &ws));
+            done = ws->sync + kSyncSoftmaxDone;
+        }
+        k_softmax_xent_rows<<<grid, kThreads, smem, s>>>(input, truth, n, batch, temp, output, delta, err, row_loss,
+                                                         cost, done);
+        return after_launch(s, "softmax_xent");
     }
+    k_softmax_xent<<<rows_grid(batch, ds), kThreads, 0, s>>>(input, truth, n, batch, temp, output, delta, err,
+                                                             row_loss);
     DNB_TRY(after_launch(s, "softmax_xent"));
     if (cost) {
         k_cost<<<1, 1024, 0, s>>>(row_loss, batch, cost);
