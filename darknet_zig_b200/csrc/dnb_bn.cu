@@ -1253,10 +1253,12 @@ dnb_status dnb_bn_act_forward_train(const float *x, float *y, float *x_norm, int
         a.rmean = rolling_mean;
         a.rvar = rolling_variance;
         bool launched = false;
-        if (!cluster_disabled())
-            DNB_TRY((run_cluster<false, false>(batch, filters, spatial, act, a, s, &launched, what, nullptr)));
+        if (!small_disabled()) DNB_TRY((run_small<false, false>(batch, filters, spatial, act, a, s, &launched, what)));
         if (launched) return DNB_OK;
         DNB_TRY((run_sweep<false, false>(batch, filters, spatial, act, a, s, &launched, what)));
+        if (launched) return DNB_OK;
+        if (!cluster_disabled())
+            DNB_TRY((run_cluster<false, false>(batch, filters, spatial, act, a, s, &launched, what, nullptr)));
         if (launched) return DNB_OK;
         if (!stage_disabled()) DNB_TRY((run_stage<false, false>(batch, filters, spatial, act, a, s, &launched, what,
                                                                 nullptr)));
@@ -1299,6 +1301,18 @@ dnb_status dnb_bn_act_backward(const float *x, const float *y, const float *delt
         a.mean_delta = mean_delta;
         a.var_delta = variance_delta;
         bool launched = false;
+        if (!small_disabled()) {
+            if (y)
+                DNB_TRY((run_small<true, true>(batch, filters, spatial, act, a, s, &launched, what)));
+            else
+                DNB_TRY((run_small<true, false>(batch, filters, spatial, act, a, s, &launched, what)));
+            if (launched) return DNB_OK;
+        }
+        if (y)
+            DNB_TRY((run_sweep<true, true>(batch, filters, spatial, act, a, s, &launched, what)));
+        else
+            DNB_TRY((run_sweep<true, false>(batch, filters, spatial, act, a, s, &launched, what)));
+        if (launched) return DNB_OK;
         if (!cluster_disabled()) {
             if (y)
                 DNB_TRY((run_cluster<true, true>(batch, filters, spatial, act, a, s, &launched, what, nullptr)));
@@ -1306,10 +1320,6 @@ dnb_status dnb_bn_act_backward(const float *x, const float *y, const float *delt
                 DNB_TRY((run_cluster<true, false>(batch, filters, spatial, act, a, s, &launched, what, nullptr)));
             if (launched) return DNB_OK;
         }
-        if (y)
-            DNB_TRY((run_sweep<true, true>(batch, filters, spatial, act, a, s, &launched, what)));
-        else
-            DNB_TRY((run_sweep<true, false>(batch, filters, spatial, act, a, s, &launched, what)));
         if (!launched && !stage_disabled()) {
             if (y)
                 DNB_TRY((run_stage<true, true>(batch, filters, spatial, act, a, s, &launched, what, nullptr)));
@@ -1354,10 +1364,9 @@ dnb_status dnb_syncbn_act_forward_train(dnb_comm comm, const float *x, float *y,
     a.rmean = rolling_mean;
     a.rvar = rolling_variance;
     bool launched = false;
-    if (!cluster_disabled())
+    DNB_TRY((run_sweep<false, false>(batch, filters, spatial, act, a, as_stream(stream), &launched, what, &cv)));
+    if (!launched && !cluster_disabled())
         DNB_TRY((run_cluster<false, false>(batch, filters, spatial, act, a, as_stream(stream), &launched, what, &cv)));
-    if (!launched)
-        DNB_TRY((run_sweep<false, false>(batch, filters, spatial, act, a, as_stream(stream), &launched, what, &cv)));
     if (!launched && !stage_disabled())
         DNB_TRY((run_stage<false, false>(batch, filters, spatial, act, a, as_stream(stream), &launched, what, &cv)));
     if (!launched) return fail(DNB_ERR_UNSUPPORTED, "%s: shape not taken by the fused kernel", what);
@@ -1397,17 +1406,15 @@ dnb_status dnb_syncbn_act_backward(dnb_comm comm, const float *x, const float *y
     a.var_delta = variance_delta;
     bool launched = false;
     const cudaStream_t s = as_stream(stream);
-    if (!cluster_disabled()) {
+    if (y)
+        DNB_TRY((run_sweep<true, true>(batch, filters, spatial, act, a, s, &launched, what, &cv)));
+    else
+        DNB_TRY((run_sweep<true, false>(batch, filters, spatial, act, a, s, &launched, what, &cv)));
+    if (!launched && !cluster_disabled()) {
         if (y)
             DNB_TRY((run_cluster<true, true>(batch, filters, spatial, act, a, s, &launched, what, &cv)));
         else
             DNB_TRY((run_cluster<true, false>(batch, filters, spatial, act, a, s, &launched, what, &cv)));
-    }
-    if (!launched) {
-        if (y)
-            DNB_TRY((run_sweep<true, true>(batch, filters, spatial, act, a, s, &launched, what, &cv)));
-        else
-            DNB_TRY((run_sweep<true, false>(batch, filters, spatial, act, a, s, &launched, what, &cv)));
     }
     if (!launched && !stage_disabled()) {
         if (y)

@@ -39,6 +39,13 @@ dnb_status run_cluster(int64_t batch, int64_t filters, int64_t spatial, int act,
                        bool *launched, const char *what, const CommView *cv);
 // DNB_BN_CLUSTER=0 turns the cluster kernel off.
 bool cluster_disabled();
+// Launches the channel-per-CTA kernel for small channels (dnb_bn_small.cu) when a channel's
+// inputs fit its shared memory; single GPU only.
+template <bool BWD, bool HASY>
+dnb_status run_small(int64_t batch, int64_t filters, int64_t spatial, int act, const BnIO &io, cudaStream_t stream,
+                     bool *launched, const char *what);
+// DNB_BN_SMALL=0 turns the small-channel kernel off.
+bool small_disabled();
 
 namespace {
 

@@ -565,7 +565,9 @@ struct Clu {
         for (int j = 0; j < J; ++j) {
             const int b = j % kCRing;
             const int64_t c = (int64_t)k + (int64_t)j * a.nc;
-            if (n_units > (uint32_t)wa && !wait_chan(a, s, s.rbar, j)) break;
+            // every output warp waits for the channel's parameters, also one without units:
+            // its arrival on abar below must not count towards an earlier channel's phase
+            if (!wait_chan(a, s, s.rbar, j)) break;
             bool ok = true;
             for (uint32_t u = wa; u < n_units; u += kCApply) {
                 const uint32_t i = i0 + u, slot = i % (uint32_t)a.R;

@@ -652,7 +652,10 @@ struct Stage {
             const Share sh = share_of(a, g, rid, a.f_ps);
             const int b = g % kTGroupRing;
             const uint32_t n_units = sh.t1 - sh.t0;
-            if (n_units > (uint32_t)wa && !wait_group(a, s, s.rbar, g)) break;
+            // every output warp waits for the group's parameters, also one without units in it:
+            // its arrival on abar below must not count towards an earlier group's phase (the
+            // producer reuses the group's state buffer once that phase completes)
+            if (!wait_group(a, s, s.rbar, g)) break;
             bool ok = true;
             for (uint32_t u = wa; u < n_units; u += kTApply) {
                 const uint32_t i = i0 + u, slot = i % (uint32_t)a.R;

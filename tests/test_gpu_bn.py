@@ -41,14 +41,15 @@ SHAPES = [
 FULL_SHAPES = [(128, 128, 1024), (128, 256, 784), (64, 128, 1024)]
 
 
-# The fused entries pick a persistent kernel (the cluster-per-channel kernel, else the L2
-# sweep, else the grid-wide shared-memory-staged kernel), else the generic multi-launch path;
-# the library reads these switches at every call, so each test below runs each path on the
-# same inputs.
+# The fused entries pick, in order: the channel-per-CTA kernel for small channels, the L2
+# sweep, the cluster-per-channel kernel, the grid-wide shared-memory-staged kernel, and the
+# generic multi-launch path. The library reads these switches at every call, so each test
+# below runs each path on the same inputs ("default" is the order itself).
 BN_PATHS = {
-    "cluster": {},
-    "sweep": {"DNB_BN_CLUSTER": "0", "DNB_BN_STAGE": "0"},
-    "stage": {"DNB_BN_CLUSTER": "0", "DNB_BN_SWEEP": "0"},
+    "default": {},
+    "sweep": {"DNB_BN_SMALL": "0", "DNB_BN_CLUSTER": "0", "DNB_BN_STAGE": "0"},
+    "cluster": {"DNB_BN_SMALL": "0", "DNB_BN_SWEEP": "0"},
+    "stage": {"DNB_BN_SMALL": "0", "DNB_BN_CLUSTER": "0", "DNB_BN_SWEEP": "0"},
     "generic": {"DNB_BN_PERSISTENT": "0"},
 }
 
