@@ -422,14 +422,15 @@ def run_ours(a):
         sd = torch.randn(E, generator=g, device=dev)
         sets.append((sx, sd, torch.empty_like(sx), torch.empty_like(sx)))
     x, delta, y, dx = sets[0]
-    gamma = torch.rand(C, generator=g, device=dev) + 0.5
-    beta = torch.randn(C, generator=g, device=dev) * 0.1
-    mean, var, bu, su, md, vd = (torch.zeros(C, device=dev) for _ in range(6))
-    rm = torch.randn(C, generator=g, device=dev) * 0.5
-    rv = torch.rand(C, generator=g, device=dev) * 1.5 + 0.5
-    # the weights are replicated: the same values on every rank
+    # the layer's parameters and running statistics are replicated, as in data-parallel
+    # training: the same values on every rank (only the batch shards differ)
     gw = torch.Generator(device=dev)
     gw.manual_seed(99)
+    gamma = torch.rand(C, generator=gw, device=dev) + 0.5
+    beta = torch.randn(C, generator=gw, device=dev) * 0.1
+    mean, var, bu, su, md, vd = (torch.zeros(C, device=dev) for _ in range(6))
+    rm = torch.randn(C, generator=gw, device=dev) * 0.5
+    rv = torch.rand(C, generator=gw, device=dev) * 1.5 + 0.5
     wts = torch.randn(NW, generator=gw, device=dev) * 0.01 if NW else None
     wup = torch.randn(NW, generator=gw, device=dev) * 1e-3 if NW else None
     flush_buf = torch.ones(64 << 20, dtype=torch.float32, device=dev) if not back_to_back else None
@@ -584,7 +585,7 @@ def run_ours(a):
         "scaling": "weak",
         "vs_baseline": None,
         "dtype": "f32",
-        "data": "synthetic (torch.randn / rand, seeded per rank; weights identical on every rank)",
+        "data": "synthetic (torch.randn / rand; batch shards seeded per rank, parameters and weights identical on every rank)",
         "parity": parity,
         "config": {"workload": workload_desc(a, world), "baseline_config": a.config, "batch_per_gpu": B,
                    "channels": C, "hw": [H, W], "global_batch": B * world, "activation": "leaky 0.1",
