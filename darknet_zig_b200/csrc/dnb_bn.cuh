@@ -193,36 +193,9 @@ __device__ __forceinline__ int owner_of(const Args &a, int g, uint32_t t, int pa
     return (int)fd.div((t + 1) * (uint32_t)parts - 1);
 }
 
-// t / d rounded to nearest even, for a divisor d > 0 that is the same for a whole launch,
-// given r = RN(1/d) computed once (on the host, by IEEE division). The divisions of
-// normalize_delta's second term (blas.zig:200) share one divisor, so the per-element
-// reciprocal of a general division is not needed:
-//   q0 = RN(t * r) is within 2 ulps of t/d; one correction step with the residual,
-//   q1 = q0 + RN(t - q0 d) * r (Markstein's division step, P. Markstein, "Computation of
-//   elementary functions on the IBM RISC System/6000 processor", IBM J. Res. Dev. 34(1),
-//   1990), leaves q1 within one ulp of t/d, so RN(t/d) is q1 or its neighbour q2 on the side
-//   of t/d. With q1 and q2 within one ulp, the residuals t - q d are exact (one fused
-//   multiply-add each), and the nearer of q1, q2 is the one with the smaller residual. The
-//   quotient of two floats never lies exactly halfway between two floats unless d is a power
-//   of two (the caller multiplies then), so there are no ties.
-// Outside |t| in [2^-80, 2^96] (zero, subnormal or huge quotients and residuals, inf, NaN)
-// the plain IEEE division is used. Tested bit for bit against IEEE division.
-__device__ __forceinline__ float div_by_const(float t, float d, float r) {
-    const float at = fabsf(t);
-    if (!(at >= 0x1p-80f && at <= 0x1p96f)) return t / d;
-    const float q0 = t * r;
-    const float q1 = __fmaf_rn(__fmaf_rn(-q0, d, t), r, q0);
-    const float r1 = __fmaf_rn(-q1, d, t);
-    // one step towards t/d: away from zero when t/d and q1 lie on the same side of q1
-    const int step = (r1 > 0.0f) == (q1 > 0.0f) ? 1 : -1;
-    const float q2 = __int_as_float(__float_as_int(q1) + step);
-    const float r2 = __fmaf_rn(-q2, d, t);
-    return fabsf(r2) < fabsf(r1) ? q2 : q1;
-}
-
 template <class Args>
 __device__ __forceinline__ float div_denom(float v, const Args &a) {
-    return a.denom_pow2 ? v * a.inv_denom : div_by_const(v, a.denom, a.inv_denom);
+    return a.denom_pow2 ? v * a.inv_denom : v / a.denom;
 }
 // dx as bn_dx1, with the division by a power-of-two denominator done as an exact multiply
 template <class Args>
