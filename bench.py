@@ -104,6 +104,9 @@ def parse(argv=None):
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-parity", action="store_true", help="skip the pre-timing parity check")
+    ap.add_argument("--full-dp", action="store_true",
+                    help="instead of the step: the data-parallel weight update of config 4 (gradient "
+                         "reduce-scatter, fused SGD on each rank's shard, all-gather of the weights)")
     a = ap.parse_args(argv)
     a.warmup = max(a.warmup, 3)
     cfg = CONFIGS[a.config]
@@ -994,8 +997,145 @@ def run_ops(a):
           lambda t: gpu.axpy(n, 0.5, t[0], t[1]))
 
 
+def run_full_dp(a):
+    """Config 4's weight update in full data parallelism (darknet_zig_b200/dpsgd.py): each
+    step reduce-scatters the ranks' gradients of the 64 Mi-float weight vector (NCCL), adds
+    this rank's shard into its momentum shard and applies the fused SGD to it (this
+    library's kernels), and all-gathers the updated weights (NCCL). Before timing one step
+    is checked: weights bit-identical on every rank, and a sample of 2048 weights equal to
+    the update with the gradients summed in float32 in rank order (exact for two ranks; within
+    1e-6 relative for more, whose sum order NCCL chooses)."""
+    import datetime
+
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    from darknet_zig_b200 import gpu
+    from darknet_zig_b200.dpsgd import ShardedSGD
+
+    gpu.init(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as td
+
+        td.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+        dist = td
+    dev = torch.device("cuda", local)
+    n = a.sgd_weights or (64 << 20)
+    batch = a.shape[0] * world
+    opt = ShardedSGD(n, world, rank, dist=dist, device=dev)
+    gw = torch.Generator(device=dev)
+    gw.manual_seed(99)
+    w = opt.padded(torch.randn(n, generator=gw, device=dev) * 0.01)
+    gr = torch.Generator(device=dev)
+    gr.manual_seed(500 + rank)
+    grads = [opt.padded(torch.randn(n, generator=gr, device=dev) * 1e-3) for _ in range(2)]
+    # one checked step
+    idx = torch.from_numpy(np.sort(np.random.default_rng(3).choice(n, size=2048, replace=False))).to(dev)
+    w0 = w[idx].cpu().numpy()
+    g_all = [torch.empty(2048, device=dev) for _ in range(world)]
+    if dist:
+        dist.all_gather(g_all, grads[0][idx].contiguous())
+    else:
+        g_all = [grads[0][idx]]
+    g_sum = np.zeros(2048, np.float32)
+    for gq in g_all:
+        g_sum = (g_sum + gq.cpu().numpy()).astype(np.float32)
+    opt.step(w, grads[0], SGD_LR, SGD_MOMENTUM, SGD_DECAY, batch)
+    torch.cuda.synchronize()
+    fails = []
+    w1 = w[idx].cpu().numpy()
+    b32 = np.float32(batch)
+    a_decay = np.float32(-np.float32(SGD_DECAY) * b32)
+    a_lr = np.float32(np.float32(SGD_LR) / b32)
+    bad = 0
+    for k in range(2048):
+        u1 = fma_f32(a_decay, w0[k], g_sum[k])  # the momentum shard starts at 0: wu = sum of gradients
+        want = fma_f32(a_lr, u1, w0[k])
+        if world <= 2:
+            bad += int(np.float32(want).view(np.uint32) != w1[k].view(np.uint32))
+        else:
+            bad += int(abs(float(want) - float(w1[k])) > 1e-6 * max(abs(float(want)), 1e-30))
+    if bad:
+        fails.append(f"{bad} of 2048 sampled weights off the expected update")
+    if dist:
+        hs = torch.tensor([float(w1.astype(np.float64).sum())], device=dev, dtype=torch.float64)
+        allh = [torch.empty_like(hs) for _ in range(world)]
+        dist.all_gather(allh, hs)
+        if any(not torch.equal(h, allh[0]) for h in allh):
+            fails.append("weights differ between ranks")
+        ok = torch.tensor([0 if fails else 1], device=dev)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+        passed = bool(ok.item())
+    else:
+        passed = not fails
+    for k in range(a.warmup):
+        opt.step(w, grads[k % 2], SGD_LR, SGD_MOMENTUM, SGD_DECAY, batch)
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    clocks = ClockSampler(local)
+    clocks.start()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    torch.cuda._sleep(int(1e-3 * 2e9) * max(1, a.steps // 4))
+    l0 = gpu.launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for k in range(a.steps):
+        opt.step(w, grads[k % 2], SGD_LR, SGD_MOMENTUM, SGD_DECAY, batch)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    launches = gpu.launch_count() - l0
+    ms = e0.elapsed_time(e1) / a.steps
+    clk = clocks.stop()
+    if dist:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    shard = opt.shard
+    line = {
+        "metric": "full data-parallel weight update of the layer's 64 Mi weights (gradient reduce-scatter, "
+                  "fused SGD on each rank's shard, weight all-gather): weights updated per second",
+        "value": round(n / (ms * 1e-3), 1),
+        "unit": "weights/s",
+        "n_gpus": world,
+        "steps": a.steps,
+        "warmup": a.warmup,
+        "ms_per_step": round(ms, 5),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (torch.randn; gradients seeded per rank, weights identical on every rank)",
+        "parity": "ok" if passed else "failed: " + "; ".join(fails or ["on another rank"]),
+        "config": {"workload": f"BASELINE cfg4 weight update, full data parallelism over {world} GPU(s): "
+                               f"NCCL reduce-scatter of {n} fp32 gradients, dnb_axpy + dnb_sgd_momentum "
+                               f"(momentum {SGD_MOMENTUM}, decay {SGD_DECAY}, lr {SGD_LR}, global batch {batch}) "
+                               f"on {shard} weights per rank, NCCL all-gather of the weights",
+                   "momentum": "sharded (each rank keeps its 1/N)", "parallelism": f"dp{world}"},
+        "hbm_bytes_per_rank_step": 28 * shard,
+        "collective_bytes_per_rank_step": 2 * 4 * shard * (world - 1),
+        "gpu_launches": launches,
+        "clocks": clk,
+    }
+    print(json.dumps(line), flush=True)
+    if not passed:
+        raise SystemExit(1)
+
+
 def main():
     a = parse()
+    if a.full_dp:
+        run_full_dp(a)
+        return
     if a.ops:
         run_ops(a)
         return
