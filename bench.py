@@ -107,6 +107,9 @@ def parse(argv=None):
     ap.add_argument("--full-dp", action="store_true",
                     help="instead of the step: the data-parallel weight update of config 4 (gradient "
                          "reduce-scatter, fused SGD on each rank's shard, all-gather of the weights)")
+    ap.add_argument("--dp-impl", choices=["fused", "nccl"], default="fused",
+                    help="--full-dp: one kernel per rank over NVLink peer memory (fused) or NCCL "
+                         "reduce-scatter / all-gather around the library's SGD kernels (nccl)")
     a = ap.parse_args(argv)
     a.warmup = max(a.warmup, 3)
     cfg = CONFIGS[a.config]
@@ -998,13 +1001,15 @@ def run_ops(a):
 
 
 def run_full_dp(a):
-    """Config 4's weight update in full data parallelism (darknet_zig_b200/dpsgd.py): each
-    step reduce-scatters the ranks' gradients of the 64 Mi-float weight vector (NCCL), adds
-    this rank's shard into its momentum shard and applies the fused SGD to it (this
-    library's kernels), and all-gathers the updated weights (NCCL). Before timing one step
-    is checked: weights bit-identical on every rank, and a sample of 2048 weights equal to
-    the update with the gradients summed in float32 in rank order (exact for two ranks; within
-    1e-6 relative for more, whose sum order NCCL chooses)."""
+    """Config 4's weight update in full data parallelism (darknet_zig_b200/dpsgd.py) on the
+    64 Mi-float weight vector: each step sums the ranks' gradients of this rank's shard, adds
+    them into its momentum shard, applies the fused SGD, and gives every rank the updated
+    weights. --dp-impl fused: one kernel per rank over NVLink peer memory (dnb_dpsgd_step);
+    nccl: NCCL reduce-scatter, this library's axpy + SGD kernels, NCCL all-gather. Before
+    timing one step is checked: weights bit-identical on every rank, and a sample of 2048
+    weights equal to the update with the gradients summed in float32 in rank order (exact for
+    the fused kernel and for two ranks; within 1e-6 relative for NCCL with more ranks, whose
+    sum order NCCL chooses)."""
     import datetime
 
     import torch
@@ -1014,7 +1019,7 @@ def run_full_dp(a):
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     from darknet_zig_b200 import gpu
-    from darknet_zig_b200.dpsgd import ShardedSGD
+    from darknet_zig_b200.dpsgd import FusedShardedSGD, ShardedSGD
 
     gpu.init(local)
     dist = None
@@ -1026,13 +1031,30 @@ def run_full_dp(a):
     dev = torch.device("cuda", local)
     n = a.sgd_weights or (64 << 20)
     batch = a.shape[0] * world
-    opt = ShardedSGD(n, world, rank, dist=dist, device=dev)
+    fused = a.dp_impl == "fused"
     gw = torch.Generator(device=dev)
     gw.manual_seed(99)
-    w = opt.padded(torch.randn(n, generator=gw, device=dev) * 0.01)
     gr = torch.Generator(device=dev)
     gr.manual_seed(500 + rank)
-    grads = [opt.padded(torch.randn(n, generator=gr, device=dev) * 1e-3) for _ in range(2)]
+    if fused:
+        opt = FusedShardedSGD(n, world, rank, dist=dist)
+        w = opt.weights
+        w[:n].copy_(torch.randn(n, generator=gw, device=dev) * 0.01)
+        opt.grads[:n].copy_(torch.randn(n, generator=gr, device=dev) * 1e-3)
+        grads = [opt.grads, opt.grads]  # read by the step, never written: one buffer serves every step
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+
+        def do_step(g):
+            opt.step(SGD_LR, SGD_MOMENTUM, SGD_DECAY, batch)
+    else:
+        opt = ShardedSGD(n, world, rank, dist=dist, device=dev)
+        w = opt.padded(torch.randn(n, generator=gw, device=dev) * 0.01)
+        grads = [opt.padded(torch.randn(n, generator=gr, device=dev) * 1e-3) for _ in range(2)]
+
+        def do_step(g):
+            opt.step(w, g, SGD_LR, SGD_MOMENTUM, SGD_DECAY, batch)
     # one checked step
     idx = torch.from_numpy(np.sort(np.random.default_rng(3).choice(n, size=2048, replace=False))).to(dev)
     w0 = w[idx].cpu().numpy()
@@ -1044,8 +1066,9 @@ def run_full_dp(a):
     g_sum = np.zeros(2048, np.float32)
     for gq in g_all:
         g_sum = (g_sum + gq.cpu().numpy()).astype(np.float32)
-    opt.step(w, grads[0], SGD_LR, SGD_MOMENTUM, SGD_DECAY, batch)
+    do_step(grads[0])
     torch.cuda.synchronize()
+    gpu.check_device_error()
     fails = []
     w1 = w[idx].cpu().numpy()
     b32 = np.float32(batch)
@@ -1055,14 +1078,15 @@ def run_full_dp(a):
     for k in range(2048):
         u1 = fma_f32(a_decay, w0[k], g_sum[k])  # the momentum shard starts at 0: wu = sum of gradients
         want = fma_f32(a_lr, u1, w0[k])
-        if world <= 2:
+        if world <= 2 or fused:
             bad += int(np.float32(want).view(np.uint32) != w1[k].view(np.uint32))
         else:
             bad += int(abs(float(want) - float(w1[k])) > 1e-6 * max(abs(float(want)), 1e-30))
     if bad:
         fails.append(f"{bad} of 2048 sampled weights off the expected update")
     if dist:
-        hs = torch.tensor([float(w1.astype(np.float64).sum())], device=dev, dtype=torch.float64)
+        # a checksum of every weight's bits
+        hs = w[:n].view(torch.int32).to(torch.int64).sum().reshape(1)
         allh = [torch.empty_like(hs) for _ in range(world)]
         dist.all_gather(allh, hs)
         if any(not torch.equal(h, allh[0]) for h in allh):
@@ -1073,7 +1097,7 @@ def run_full_dp(a):
     else:
         passed = not fails
     for k in range(a.warmup):
-        opt.step(w, grads[k % 2], SGD_LR, SGD_MOMENTUM, SGD_DECAY, batch)
+        do_step(grads[k % 2])
     torch.cuda.synchronize()
     stream = torch.cuda.current_stream()
     clocks = ClockSampler(local)
@@ -1086,12 +1110,15 @@ def run_full_dp(a):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for k in range(a.steps):
-        opt.step(w, grads[k % 2], SGD_LR, SGD_MOMENTUM, SGD_DECAY, batch)
+        do_step(grads[k % 2])
     e1.record(stream)
     torch.cuda.synchronize()
     launches = gpu.launch_count() - l0
     ms = e0.elapsed_time(e1) / a.steps
     clk = clocks.stop()
+    gpu.check_device_error()
+    if fused:
+        opt.close()
     if dist:
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -1104,6 +1131,8 @@ def run_full_dp(a):
     line = {
         "metric": "full data-parallel weight update of the layer's 64 Mi weights (gradient reduce-scatter, "
                   "fused SGD on each rank's shard, weight all-gather): weights updated per second",
+        "impl_variant": ("one kernel per rank over NVLink peer memory (dnb_dpsgd_step)" if fused else
+                         "NCCL reduce-scatter + dnb_axpy + dnb_sgd_momentum + NCCL all-gather"),
         "value": round(n / (ms * 1e-3), 1),
         "unit": "weights/s",
         "n_gpus": world,
@@ -1117,9 +1146,10 @@ def run_full_dp(a):
         "data": "synthetic (torch.randn; gradients seeded per rank, weights identical on every rank)",
         "parity": "ok" if passed else "failed: " + "; ".join(fails or ["on another rank"]),
         "config": {"workload": f"BASELINE cfg4 weight update, full data parallelism over {world} GPU(s): "
-                               f"NCCL reduce-scatter of {n} fp32 gradients, dnb_axpy + dnb_sgd_momentum "
+                               f"{n} fp32 gradients summed over the ranks shard by shard, momentum SGD "
                                f"(momentum {SGD_MOMENTUM}, decay {SGD_DECAY}, lr {SGD_LR}, global batch {batch}) "
-                               f"on {shard} weights per rank, NCCL all-gather of the weights",
+                               f"on {shard} weights per rank, the weights gathered on every rank "
+                               f"({'fused kernel over NVLink' if fused else 'NCCL collectives'})",
                    "momentum": "sharded (each rank keeps its 1/N)", "parallelism": f"dp{world}"},
         "hbm_bytes_per_rank_step": 28 * shard,
         "collective_bytes_per_rank_step": 2 * 4 * shard * (world - 1),

@@ -23,6 +23,7 @@ _CTYPES = {
     "size_t": C.c_size_t,
     "dnb_stream": C.c_void_p,
     "dnb_comm": C.c_void_p,
+    "dnb_dpsgd": C.c_void_p,
     "dnb_status": C.c_int,
 }
 

@@ -12,9 +12,15 @@ rank's gradient. Here each rank owns 1/N of the weight vector's update (ZeRO sta
     all-gather of the updated weight shards         every rank holds the same weights
 
 The momentum state (weight_updates) stays sharded: each rank keeps only its 1/N. Every rank
-ends with bit-identical weights, since each shard is computed once and broadcast. The
-collectives go through a torch.distributed process group (NCCL on GPUs; the same host logic
-runs over gloo on the CPU in tests/test_dpsgd_cpu.py with the update supplied by the caller).
+ends with bit-identical weights, since each shard is computed once and broadcast.
+
+ShardedSGD runs the three steps as NCCL collectives around this library's kernels (through a
+torch.distributed process group; the same host logic runs over gloo on the CPU in
+tests/test_dpsgd_cpu.py with the update supplied by the caller). FusedShardedSGD does all
+three in one kernel per rank over NVLink peer memory (dnb_dpsgd_*): each rank reads its
+shard's gradients from every rank, updates the shard and stores the new weights into every
+rank's weight vector, element by element; the weights and gradients then live in the
+library's shared buffers.
 """
 from __future__ import annotations
 
@@ -70,3 +76,38 @@ class ShardedSGD:
             # NCCL gathers in place (the shard is this rank's slice of the output); gloo wants
             # a separate input
             d.all_gather_into_tensor(weights_pad, w_shard if w_shard.is_cuda else w_shard.clone())
+
+
+class FusedShardedSGD:
+    """The same update as ShardedSGD in one kernel per rank over NVLink peer memory. The
+    weight vector and the gradient buffer are the library's (`weights`, `grads`: torch
+    views of n_pad floats); the host swaps the group's IPC handles once through `dist`."""
+
+    def __init__(self, n: int, world: int, rank: int, dist=None):
+        import torch
+
+        from . import gpu
+
+        if world > 1 and dist is None:
+            raise ValueError("world > 1 needs a torch.distributed module with an initialised process group")
+        self.n, self.world, self.rank = n, world, rank
+        self.group, handle, self.weights, self.grads, self.lo, self.shard = gpu.dpsgdInit(rank, world, n)
+        handles = [handle]
+        if world > 1:
+            handles = [None] * world
+            dist.all_gather_object(handles, handle)
+        gpu.dpsgdConnect(self.group, b"".join(handles))
+        self.n_pad = self.shard * world
+        self.momentum = torch.zeros(self.shard, dtype=torch.float32, device="cuda")
+
+    def step(self, learning_rate, momentum, decay, batch) -> None:
+        from . import gpu
+
+        gpu.dpsgdStep(self.group, self.momentum, learning_rate, momentum, decay, batch)
+
+    def close(self) -> None:
+        from . import gpu
+
+        if self.group is not None:
+            gpu.dpsgdDestroy(self.group)
+            self.group = None

@@ -282,3 +282,51 @@ def syncbnActBackward(comm, x, y, delta, dx, batch, filters, spatial, scales, bi
          int(spatial), _p(scales), _p(biases), _p(mean_in), _p(variance_in), _p(bias_updates), _p(scale_updates),
          _p(mean_delta_out), _p(variance_delta_out), int(act), _s())
 
+
+
+# ---- data-parallel weight update over NVLink (no reference counterpart) -----------------
+
+class _DeviceArray:
+    """A float32 device vector owned by the library, seen by torch through
+    __cuda_array_interface__ (no copy)."""
+
+    def __init__(self, ptr: int, n: int):
+        self.__cuda_array_interface__ = {"shape": (int(n),), "typestr": "<f4", "data": (int(ptr), False),
+                                         "version": 3, "strides": None}
+
+
+def dpsgdInit(rank: int, world: int, n: int):  # noqa: N802
+    """A data-parallel update group on the current device: (group, 64-byte IPC handle,
+    weights, gradients, shard_lo, shard_n); weights and gradients are torch views of the
+    library's shared vectors (padded length world * shard_n)."""
+    import ctypes
+
+    group = ctypes.c_void_p(0)
+    ipc = ctypes.create_string_buffer(64)
+    w, g = ctypes.c_void_p(0), ctypes.c_void_p(0)
+    lo, sn = ctypes.c_int64(0), ctypes.c_int64(0)
+    call("dpsgd_init", int(rank), int(world), int(n), ipc, ctypes.byref(w), ctypes.byref(g), ctypes.byref(lo),
+         ctypes.byref(sn), ctypes.byref(group))
+    n_pad = sn.value * world
+    wt = torch.as_tensor(_DeviceArray(w.value, n_pad), device="cuda")
+    gt = torch.as_tensor(_DeviceArray(g.value, n_pad), device="cuda")
+    return group.value, ipc.raw, wt, gt, lo.value, sn.value
+
+
+def dpsgdConnect(group, handles: bytes) -> None:  # noqa: N802
+    import ctypes
+
+    call("dpsgd_connect", ctypes.c_void_p(group), ctypes.create_string_buffer(bytes(handles), len(handles)))
+
+
+def dpsgdStep(group, momentum, learning_rate, momentum_coef, decay, batch) -> None:  # noqa: N802
+    import ctypes
+
+    call("dpsgd_step", ctypes.c_void_p(group), _p(momentum), float(learning_rate), float(momentum_coef),
+         float(decay), int(batch), _s())
+
+
+def dpsgdDestroy(group) -> None:  # noqa: N802
+    import ctypes
+
+    call("dpsgd_destroy", ctypes.c_void_p(group))

@@ -35,6 +35,7 @@ extern "C" {
 typedef int dnb_status;
 typedef void *dnb_stream; /* a cudaStream_t / CUstream; NULL = legacy default stream */
 typedef void *dnb_comm;   /* a sync-BN communicator (dnb_comm_init); NULL = none */
+typedef void *dnb_dpsgd;  /* a data-parallel weight-update group (dnb_dpsgd_init) */
 
 enum {
     DNB_OK = 0,
@@ -279,9 +280,9 @@ dnb_status dnb_comm_destroy(dnb_comm comm);
 /* dnb_bn_act_forward_train with the statistics of the whole data-parallel batch: every rank
  * passes its shard (the same batch, filters and spatial on every rank) and gets identical
  * mean, variance and rolling statistics. Every rank must make the same sequence of fused
- * sync-BN calls on a communicator, from one host thread per rank. Needs spatial % 4 == 0,
- * 16-byte aligned tensors and filters <= max_channels; DNB_ERR_UNSUPPORTED otherwise (the
- * split entries below then apply). A rank that never makes its call leaves the others'
+ * sync-BN calls on a communicator, from one host thread per rank. Needs 16-byte aligned
+ * tensors and filters <= max_channels, and spatial % 4 == 0 or an element count that is a
+ * multiple of 4; DNB_ERR_UNSUPPORTED otherwise (the split entries below then apply). A rank that never makes its call leaves the others'
  * kernels waiting until the wait limit; they return DNB_ERR_TIMEOUT. The records a call
  * exchanges are tagged with its call number, which repeats after 2^32 - 1 fused calls on one
  * communicator: recreate the communicator before then. */
@@ -296,6 +297,35 @@ dnb_status dnb_syncbn_act_backward(dnb_comm comm, const float *x, const float *y
                                    const float *biases, const float *mean, const float *variance,
                                    float *bias_updates, float *scale_updates, float *mean_delta,
                                    float *variance_delta, int act, dnb_stream stream);
+
+/* ------------------------------------------------------------------------------------ */
+/* data-parallel weight update: no counterpart in the reference (it trains on one GPU);    */
+/* convolutional.zig:330-334's update with every rank's gradients summed, in one kernel    */
+/* per rank over NVLink peer memory (reduce-scatter, fused SGD on the rank's shard and     */
+/* all-gather, element by element)                                                         */
+/* ------------------------------------------------------------------------------------ */
+
+/* One process (or thread) per GPU, `world` ranks (<= 8), every rank the same n. Allocates this
+ * rank's weight vector and gradient buffer (n floats each, padded; zero-filled) in one buffer
+ * shared with the other ranks, writes its CUDA IPC handle (64 bytes) to handle_out, and returns
+ * the two vectors and this rank's shard [*shard_lo, *shard_lo + *shard_n) of the weights. The
+ * caller keeps its layer's weights and accumulates its gradients in them, and passes every
+ * rank's handle, in rank order, to dnb_dpsgd_connect on every rank (any host transport). */
+dnb_status dnb_dpsgd_init(int rank, int world, int64_t n, void *handle_out, float **weights, float **grads,
+                          int64_t *shard_lo, int64_t *shard_n, dnb_dpsgd *group);
+/* Opens the peers' buffers (handles: world x 64 bytes, rank order). */
+dnb_status dnb_dpsgd_connect(dnb_dpsgd group, const void *handles);
+/* One update on every rank: for this rank's shard, gradient = sum over ranks (rank order) of
+ * their gradient vectors, momentum += gradient, then convolutional.zig:330-334 with batch the
+ * global batch, and the new weights stored into every rank's weight vector. `momentum` is this
+ * rank's shard of weight_updates (*shard_n floats, 16-byte aligned, zero before the first
+ * step). Every rank must make the same calls; on return of the stream work every rank holds
+ * identical weights, and the gradient vectors may be overwritten. A rank that never calls
+ * leaves the others waiting until the wait limit (DNB_ERR_TIMEOUT from
+ * dnb_check_device_error); recreate the group on every rank then. */
+dnb_status dnb_dpsgd_step(dnb_dpsgd group, float *momentum, float learning_rate, float momentum_coef, float decay,
+                          int64_t batch, dnb_stream stream);
+dnb_status dnb_dpsgd_destroy(dnb_dpsgd group);
 
 /* ------------------------------------------------------------------------------------ */
 /* sync-BN across GPUs (the reference has no multi-GPU support, README.md:313-317).        */
