@@ -13,6 +13,7 @@ from __future__ import annotations
 import concurrent.futures as cf
 import glob
 import os
+import shutil
 import subprocess
 import sys
 
@@ -23,7 +24,22 @@ INCLUDE = os.path.join(ROOT, "include")
 OBJ = os.path.join(PKG, "_build")
 LIB = os.path.join(PKG, "libdnb200.so")
 
-NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
+
+
+def find_nvcc() -> str:
+    """nvcc from $NVCC, else $CUDA_HOME / $CUDA_PATH, else the PATH."""
+    if os.environ.get("NVCC"):
+        return os.environ["NVCC"]
+    for var in ("CUDA_HOME", "CUDA_PATH"):
+        home = os.environ.get(var)
+        if home and os.path.exists(os.path.join(home, "bin", "nvcc")):
+            return os.path.join(home, "bin", "nvcc")
+    found = shutil.which("nvcc")
+    if not found:
+        raise RuntimeError("nvcc not found: set NVCC or CUDA_HOME, or put nvcc on the PATH")
+    return found
+
+
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-std=c++20", *ARCH, "-O3", "-lineinfo", "--fmad=false", "-Xcompiler", "-fPIC,-O2",
          "-I", INCLUDE, "-I", CSRC]
@@ -43,7 +59,7 @@ def _newer(out: str, deps: list[str]) -> bool:
 def _compile(src: str, force: bool) -> str:
     obj = os.path.join(OBJ, os.path.basename(src)[:-3] + ".o")
     if force or _newer(obj, [src, __file__, *_headers()]):
-        cmd = [NVCC, *FLAGS, "-c", src, "-o", obj]
+        cmd = [find_nvcc(), *FLAGS, "-c", src, "-o", obj]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"nvcc failed for {src}:\n{r.stdout}\n{r.stderr}")
@@ -56,7 +72,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
     with cf.ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 1)) as ex:
         objs = list(ex.map(lambda s: _compile(s, force), sources))
     if force or _newer(LIB, objs):
-        cmd = [NVCC, *ARCH, "-shared", "-cudart", "static", "-o", LIB, *objs]
+        cmd = [find_nvcc(), *ARCH, "-shared", "-cudart", "static", "-o", LIB, *objs]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")

@@ -98,8 +98,9 @@ def build_ref_gpu(force: bool = False) -> str | None:
     src = os.path.join(HERE, "ref_gpu.cu")
     os.makedirs(REF_OUT, exist_ok=True)
     if force or _stale(REF_GPU_SO, [src, REFERENCE_KERNELS, __file__]):
-        nvcc = os.path.join(os.environ.get("CUDA_HOME", "/usr/local/cuda"), "bin", "nvcc")
-        cmd = [nvcc if os.path.exists(nvcc) else "nvcc", "-x", "cu", "-O3",
+        home = os.environ.get("CUDA_HOME") or os.environ.get("CUDA_PATH") or ""
+        nvcc = os.environ.get("NVCC") or os.path.join(home, "bin", "nvcc")
+        cmd = [nvcc if home or os.environ.get("NVCC") else "nvcc", "-x", "cu", "-O3",
                "-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo", "-Wno-deprecated-gpu-targets",
                "-shared", "-Xcompiler", "-fPIC", f"-DDNB_REFERENCE_KERNELS=\"{REFERENCE_KERNELS}\"",
                "-o", REF_GPU_SO, src]
