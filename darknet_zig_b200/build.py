@@ -26,15 +26,19 @@ LIB = os.path.join(PKG, "libdnb200.so")
 
 
 
-def find_nvcc() -> str:
-    """nvcc from $NVCC, else $CUDA_HOME / $CUDA_PATH, else the PATH."""
+def nvcc_path() -> str | None:
+    """nvcc from $NVCC, else $CUDA_HOME / $CUDA_PATH, else the PATH; None if there is none."""
     if os.environ.get("NVCC"):
         return os.environ["NVCC"]
     for var in ("CUDA_HOME", "CUDA_PATH"):
         home = os.environ.get(var)
         if home and os.path.exists(os.path.join(home, "bin", "nvcc")):
             return os.path.join(home, "bin", "nvcc")
-    found = shutil.which("nvcc")
+    return shutil.which("nvcc")
+
+
+def find_nvcc() -> str:
+    found = nvcc_path()
     if not found:
         raise RuntimeError("nvcc not found: set NVCC or CUDA_HOME, or put nvcc on the PATH")
     return found

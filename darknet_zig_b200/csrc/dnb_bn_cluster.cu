@@ -326,6 +326,12 @@ struct Clu {
             // a warp without units would otherwise overwrite wpart of channel j - kCRing
             // before the exchange warp has read it
             if (j >= kCRing && !wait_chan(a, s, s.rbar, j - kCRing)) return;
+            // every statistics warp is done with channel j - 1, so every unit of the earlier
+            // channels has landed: the previous occupant of each slot this warp waits on
+            // below. Without it a warp running a channel ahead could test a slot's `full`
+            // barrier while the phase of the slot's previous unit is still open, and a parity
+            // wait one phase early succeeds at once (stale data in the sums).
+            if (j >= 1 && !wait_chan(a, s, s.sbar, j - 1)) return;
             const int64_t c = (int64_t)k + (int64_t)j * a.nc;
             float s1 = 0.0f, s2 = 0.0f;
             if constexpr (!BWD) {

@@ -332,6 +332,12 @@ struct Stage {
             // a warp without units in the groups ahead would otherwise reach group g while the
             // publisher still reads group g - kTGroupRing's partials from the same buffer
             if (g >= kTGroupRing && !wait_group(a, s, s.pbar, g - kTGroupRing)) return;
+            // every statistics warp is done with group g - 1, so every unit of the earlier
+            // groups has landed: the previous occupant of each slot this warp waits on below.
+            // Without it a warp running a group ahead could test a slot's `full` barrier while
+            // the phase of the slot's previous unit is still open, and a parity wait one phase
+            // early succeeds at once (stale data in the sums).
+            if (g >= 1 && !wait_group(a, s, s.sbar, g - 1)) return;
             const Share sh = share_of(a, g, rid, a.f_ps);
             const int b = g % kTGroupRing;
             const uint32_t n_units = sh.t1 - sh.t0;

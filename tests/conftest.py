@@ -58,7 +58,7 @@ def built_lib():
     library is used as is."""
     from darknet_zig_b200 import build
 
-    if os.path.exists(build.NVCC):
+    if build.nvcc_path():
         build.build()
     assert os.path.exists(build.LIB), "libdnb200.so is missing and cannot be built here"
     return build.LIB

@@ -25,12 +25,13 @@ def test_library_exports_every_declared_symbol(built_lib):
 
 def test_library_is_built_for_sm100a(built_lib):
     """The embedded device code is named for sm_100a (the file list only; the tool is the
-    one next to the nvcc the build uses, $NVCC)."""
+    one next to the nvcc the build uses)."""
     from darknet_zig_b200 import build
 
-    tool = os.path.join(os.path.dirname(build.NVCC), "cuobjdump")
-    if not os.path.exists(tool):
-        pytest.skip(f"no cuobjdump beside {build.NVCC}")
+    nvcc = build.nvcc_path()
+    tool = os.path.join(os.path.dirname(nvcc), "cuobjdump") if nvcc else ""
+    if not tool or not os.path.exists(tool):
+        pytest.skip(f"no cuobjdump beside the nvcc the build uses ({nvcc})")
     out = subprocess.run([tool, "--list-elf", built_lib], capture_output=True, text=True)
     assert "sm_100a" in out.stdout
 
