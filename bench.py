@@ -56,7 +56,6 @@ import os
 import statistics
 import subprocess
 import sys
-import threading
 import time
 from fractions import Fraction
 
@@ -160,81 +159,80 @@ def profiled_traffic():
 # ---- clocks ---------------------------------------------------------------------------
 
 class ClockSampler:
-    """SM clock and clock-event reasons sampled every ~1 ms through NVML (read-only queries)
-    from a background thread while the timed regions run; nvidia-smi once as a fallback."""
+    """SM clock and clock-event reasons during the timed regions: `nvidia-smi -lms` in its own
+    process (read-only queries; a process of its own, so no Python thread scheduling thins
+    the samples), with one NVML reading as the fallback."""
 
-    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
-               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
-               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
-               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"),
-               ("hw_power_brake_slowdown", "nvmlClocksEventReasonHwPowerBrakeSlowdown"))
+    FIELDS = ("clocks.sm", "clocks.max.sm", "clocks_event_reasons.hw_slowdown",
+              "clocks_event_reasons.hw_thermal_slowdown", "clocks_event_reasons.sw_thermal_slowdown",
+              "clocks_event_reasons.sw_power_cap")
+    REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
-    def __init__(self, gpu_index: int):
+    def __init__(self, gpu_index: int, interval_ms: int = 10):
         self.idx = gpu_index
-        self.samples = []
-        self.stop_evt = threading.Event()
-        self.thread = None
-        self.nvml = None
-        self.handle = None
+        self.interval_ms = interval_ms
+        self.proc = None
+        self.out = None
+
+    def _target(self) -> str:
+        try:
+            import torch
+
+            return "GPU-" + str(torch.cuda.get_device_properties(self.idx).uuid)
+        except Exception:
+            return str(self.idx)
 
     def start(self):
+        import tempfile
+
+        self.out = tempfile.TemporaryFile(mode="w+")
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", self._target(), "--query-gpu=" + ",".join(self.FIELDS),
+                 "--format=csv,noheader,nounits", "-lms", str(self.interval_ms)],
+                stdout=self.out, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        time.sleep(0.3)  # the first sample lands before the timed region starts
+
+    def stop(self):
+        rows = []
+        if self.proc is not None:
+            time.sleep(2 * self.interval_ms / 1000)
+            self.proc.terminate()  # the sampler started above, by its own handle
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.proc.wait()
+            self.out.seek(0)
+            for line in self.out:
+                parts = [v.strip() for v in line.split(",")]
+                if len(parts) != len(self.FIELDS):
+                    continue
+                try:
+                    rows.append((float(parts[0]), float(parts[1]), parts[2:]))
+                except ValueError:
+                    continue
+        if self.out is not None:
+            self.out.close()
+        if not rows:
+            return self._nvml_once()
+        reasons = sorted({name for _, _, flags in rows for name, f in zip(self.REASONS, flags) if f == "Active"})
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_min_mhz": min(r[0] for r in rows),
+                "sm_max_mhz": max(r[1] for r in rows), "reasons": reasons, "samples": len(rows),
+                "interval_ms": self.interval_ms, "source": "nvidia-smi -lms during the timed regions"}
+
+    def _nvml_once(self):
         try:
             import pynvml
 
             pynvml.nvmlInit()
-            uuid = None
-            try:
-                import torch
-
-                uuid = "GPU-" + str(torch.cuda.get_device_properties(self.idx).uuid)
-            except Exception:
-                pass
-            self.handle = (pynvml.nvmlDeviceGetHandleByUUID(uuid) if uuid else
-                           pynvml.nvmlDeviceGetHandleByIndex(self.idx))
-            self.nvml = pynvml
-        except Exception:
-            self.nvml = None
-            return
-        self.thread = threading.Thread(target=self._poll, daemon=True)
-        self.thread.start()
-
-    def _poll(self):
-        n = self.nvml
-        while not self.stop_evt.is_set():
-            try:
-                sm = n.nvmlDeviceGetClockInfo(self.handle, n.NVML_CLOCK_SM)
-                bits = n.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
-                self.samples.append((sm, bits))
-            except Exception:
-                break
-            time.sleep(0.001)
-
-    def stop(self):
-        if self.nvml is None:
-            return self._smi_once()
-        self.stop_evt.set()
-        self.thread.join(timeout=5)
-        n = self.nvml
-        try:
-            smax = float(n.nvmlDeviceGetMaxClockInfo(self.handle, n.NVML_CLOCK_SM))
-        except Exception:
-            smax = None
-        if not self.samples:
-            return None
-        reasons = set()
-        for _, bits in self.samples:
-            for name, const in self.REASONS:
-                if bits & getattr(n, const, 0):
-                    reasons.add(name)
-        return {"sm_mhz": statistics.median(s for s, _ in self.samples), "sm_min_mhz": min(s for s, _ in self.samples),
-                "sm_max_mhz": smax, "reasons": sorted(reasons), "samples": len(self.samples), "source": "nvml"}
-
-    def _smi_once(self):
-        try:
-            out = subprocess.run(["nvidia-smi", "--query-gpu=clocks.sm,clocks.max.sm", "--format=csv,noheader,nounits",
-                                  "-i", str(self.idx)], capture_output=True, text=True, timeout=10).stdout
-            sm, smax = (float(v) for v in out.strip().split(","))
-            return {"sm_mhz": sm, "sm_max_mhz": smax, "reasons": [], "samples": 1, "source": "nvidia-smi after"}
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.idx)
+            sm = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+            smax = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+            return {"sm_mhz": float(sm), "sm_max_mhz": float(smax), "reasons": [], "samples": 1,
+                    "source": "nvml, once after the timed regions"}
         except Exception:
             return None
 
