@@ -26,8 +26,13 @@
 // statistics the outputs are bit-identical to it.
 #include <math.h>
 
+#include <string.h>
+
 #include <algorithm>
 #include <atomic>
+#include <mutex>
+#include <utility>
+#include <vector>
 
 #include "dnb_bn.cuh"
 
@@ -373,8 +378,7 @@ struct PArgs {
     uint32_t T_full, T_last;  // units in a group (every group but the last / the last)
     FastDiv f_nk, f_k, f_ps, f_tfull, f_tlast;
     float denom;              // batch*spatial as f32 (normalize_delta's denominator)
-    float inv_denom;          // 1/denom, used only when denom is a power of two (then exact)
-    int denom_pow2;
+    ConstDiv cdiv;            // division by denom, per element
     // tensors: fwd uses t0 = x; bwd uses t0 = delta, t1 = x, t2 = y (optional)
     const float *t0, *t1, *t2;
     float *out, *xnorm;
@@ -977,11 +981,7 @@ struct SweepKernel {
                 for (int j = 0; j < UNROLL; ++j)
                     if (ok[j]) {
                         const float4 yy = HASY ? yv[j] : xv[j];
-                        st4_hint(a.out + offs[j],
-                                 make_float4(bn_dx_p(bn_grad1<A, HASY>(d[j].x, xv[j].x, yy.x, p, a.act), xv[j].x, p, a),
-                                             bn_dx_p(bn_grad1<A, HASY>(d[j].y, xv[j].y, yy.y, p, a.act), xv[j].y, p, a),
-                                             bn_dx_p(bn_grad1<A, HASY>(d[j].z, xv[j].z, yy.z, p, a.act), xv[j].z, p, a),
-                                             bn_dx_p(bn_grad1<A, HASY>(d[j].w, xv[j].w, yy.w, p, a.act), xv[j].w, p, a)),
+                        st4_hint(a.out + offs[j], bn_dx4_p(bn_grad4<A, HASY>(d[j], xv[j], yy, p, a.act), xv[j], p, a),
                                  pol);
                     }
             }
@@ -1180,10 +1180,7 @@ void fill_partition(PArgs &a, const PPlan &pl, int64_t batch, int64_t filters, i
     a.f_tfull = FastDiv(a.T_full);
     a.f_tlast = FastDiv(a.T_last);
     a.denom = (float)(spatial * batch);
-    // dividing by a power of two equals multiplying by its exact reciprocal
-    int e2 = 0;
-    a.denom_pow2 = frexpf(a.denom, &e2) == 0.5f;
-    a.inv_denom = 1.0f / a.denom;
+    a.cdiv = const_div(a.denom);
 }
 
 template <bool BWD, bool HASY>
@@ -1251,7 +1248,7 @@ dnb_status run_sweep(int64_t batch, int64_t filters, int64_t spatial, int act, c
         // the backward ran 110.2 us flat against 114.0 us per unit, the forward (whose
         // statistics pass streams at HBM speed with less arithmetic to hide the extra index
         // work behind) 65.1 us against 55.5 us
-        const bool flat = BWD && (pl.U / 4) % chunk != 0 && !flat_cut_disabled();
+        [[maybe_unused]] const bool flat = BWD && (pl.U / 4) % chunk != 0 && !flat_cut_disabled();
         a.f_u4 = FastDiv((uint32_t)(pl.U / 4));
         a.act = act;
         a.rec = ws->recs;
@@ -1274,9 +1271,7 @@ dnb_status run_sweep(int64_t batch, int64_t filters, int64_t spatial, int act, c
             for (int r = 0; r < cv->world; ++r) a.xrec[r] = cv->rec[r];
             // normalize_delta divides by the element count of the whole batch
             a.denom = (float)(batch * spatial * cv->world);
-            int e2 = 0;
-            a.denom_pow2 = frexpf(a.denom, &e2) == 0.5f;
-            a.inv_denom = 1.0f / a.denom;
+            a.cdiv = const_div(a.denom);
         }
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3((unsigned)pl.P);
@@ -1302,6 +1297,63 @@ dnb_status run_sweep(int64_t batch, int64_t filters, int64_t spatial, int act, c
 }
 
 }  // namespace
+
+// Verifies q = fma(a, zh, a * zl) against IEEE division a / d for every a in [1, 2) on the
+// host (float division and fmaf are correctly rounded there, as fma is on the device). The
+// verdict depends only on the significand of d: scaling d by 2^k scales zh and zl by 2^-k.
+// About 2^23 divisions, tens of milliseconds, once per significand and process.
+ConstDiv const_div(float d) {
+    ConstDiv k;
+    k.d = d;
+    k.lo = 0x7f800000u;  // no v takes the two-operation form until the check passes
+    if (!(d >= 1.0f) || !(d <= 0x1p40f)) return k;  // counts; zh and zl stay normal
+    k.zh = 1.0f / d;
+    k.zl = (float)(1.0 / (double)d - (double)k.zh);
+    int e2 = 0;
+    if (frexpf(d, &e2) == 0.5f) {  // 1/d is exact
+        k.pow2 = 1;
+        k.zl = 0.0f;
+        return k;
+    }
+    uint32_t dbits;
+    memcpy(&dbits, &d, 4);
+    const uint32_t key = dbits & 0x007fffffu;
+    static std::mutex mu;
+    static std::vector<std::pair<uint32_t, bool>> verdicts;
+    int known = -1;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        for (const auto &v : verdicts)
+            if (v.first == key) known = v.second ? 1 : 0;
+    }
+    if (known < 0) {
+        // the check runs on the divisor with the same significand in [1, 2)
+        int e = 0;
+        const float d1 = ldexpf(frexpf(d, &e), 1);
+        const float zh1 = 1.0f / d1;
+        const float zl1 = (float)(1.0 / (double)d1 - (double)zh1);
+        bool ok = true;
+        for (uint32_t m = 0; m < (1u << 23) && ok; ++m) {
+            const uint32_t bits = 0x3f800000u | m;
+            float a;
+            memcpy(&a, &bits, 4);
+            volatile float t = a * zl1;  // one rounding, as on the device (no contraction)
+            const float q = fmaf(a, zh1, t);
+            ok = q == a / d1;
+        }
+        std::lock_guard<std::mutex> lock(mu);
+        verdicts.emplace_back(key, ok);
+        known = ok ? 1 : 0;
+    }
+    if (!known) return k;
+    // |v| from which every intermediate is normal: |v * zl| >= 2^-126 and |v / d| >= 2^-126
+    // (factors of 2 for margin); below it, and for zero, v / d is divided
+    float lo = ldexpf(d, -124);
+    if (k.zl != 0.0f) lo = fmaxf(lo, ldexpf(1.0f, -125) / fabsf(k.zl));
+    if (lo < 0x1p127f) memcpy(&k.lo, &lo, 4);
+    return k;
+}
+
 }  // namespace dnb
 
 using namespace dnb;

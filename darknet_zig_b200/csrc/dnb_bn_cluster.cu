@@ -63,8 +63,8 @@ struct CArgs {
     int R, SU, slot_floats, vec, bulk_out;
     int pf_from;               // first channel (of a cluster's sequence) prefetched into L2
     FastDiv f_k;
-    float denom, inv_denom;    // normalize_delta's denominator (all ranks' elements)
-    int denom_pow2;
+    float denom;               // normalize_delta's denominator (all ranks' elements)
+    ConstDiv cdiv;             // division by denom, per element
     double count;              // elements behind a channel's statistics (all ranks)
     BnIO io;
     int act;
@@ -630,11 +630,7 @@ struct Clu {
                         for (int q = lane; q < n4; q += 32) {
                             const float4 d = d4[q], xv = x4[q];
                             const float4 yy = HASY ? y4[q] : xv;
-                            const float4 o4 =
-                                make_float4(bn_dx_p(bn_grad1<A, HASY>(d.x, xv.x, yy.x, p, a.act), xv.x, p, a),
-                                            bn_dx_p(bn_grad1<A, HASY>(d.y, xv.y, yy.y, p, a.act), xv.y, p, a),
-                                            bn_dx_p(bn_grad1<A, HASY>(d.z, xv.z, yy.z, p, a.act), xv.z, p, a),
-                                            bn_dx_p(bn_grad1<A, HASY>(d.w, xv.w, yy.w, p, a.act), xv.w, p, a));
+                            const float4 o4 = bn_dx4_p(bn_grad4<A, HASY>(d, xv, yy, p, a.act), xv, p, a);
                             if (a.bulk_out)
                                 d4[q] = o4;  // over delta, element by element
                             else
@@ -895,9 +891,7 @@ dnb_status run_cluster(int64_t batch, int64_t filters, int64_t spatial, int act,
         }
         a.count = (double)batch * (double)spatial * world;
         a.denom = (float)(batch * spatial * world);
-        int e2 = 0;
-        a.denom_pow2 = frexpf(a.denom, &e2) == 0.5f;
-        a.inv_denom = 1.0f / a.denom;
+        a.cdiv = const_div(a.denom);
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3((unsigned)(pl.nc * pl.Q));
         cfg.blockDim = dim3(kCThreads);

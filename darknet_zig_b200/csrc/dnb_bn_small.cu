@@ -29,8 +29,8 @@ struct SmArgs {
     int N;
     FastDiv fs;     // divide by S
     int vec;        // S % 4 == 0 and aligned tensors: float4 access
-    float denom, inv_denom;
-    int denom_pow2;
+    float denom;
+    ConstDiv cdiv;  // division by denom, per element
     BnIO io;
     int act;
 };
@@ -186,11 +186,7 @@ __global__ void __launch_bounds__(kSmThreads) k_bn_small(SmArgs a) {
                     const float4 d = reinterpret_cast<const float4 *>(ch)[e];
                     const float4 xv = reinterpret_cast<const float4 *>(ch + NS)[e];
                     const float4 yy = HASY ? reinterpret_cast<const float4 *>(ch + 2 * NS)[e] : xv;
-                    st4_stream(a.io.out + o,
-                               make_float4(bn_dx_p(bn_grad1<A, HASY>(d.x, xv.x, yy.x, p, a.act), xv.x, p, a),
-                                           bn_dx_p(bn_grad1<A, HASY>(d.y, xv.y, yy.y, p, a.act), xv.y, p, a),
-                                           bn_dx_p(bn_grad1<A, HASY>(d.z, xv.z, yy.z, p, a.act), xv.z, p, a),
-                                           bn_dx_p(bn_grad1<A, HASY>(d.w, xv.w, yy.w, p, a.act), xv.w, p, a)));
+                    st4_stream(a.io.out + o, bn_dx4_p(bn_grad4<A, HASY>(d, xv, yy, p, a.act), xv, p, a));
                 }
             } else {
                 for (int64_t e = threadIdx.x; e < NS; e += kSmThreads) {
@@ -236,9 +232,7 @@ dnb_status run_small(int64_t batch, int64_t filters, int64_t spatial, int act, c
     a.fs = FastDiv((uint32_t)spatial);
     a.vec = al && spatial % 4 == 0;
     a.denom = (float)(batch * spatial);
-    int e2 = 0;
-    a.denom_pow2 = frexpf(a.denom, &e2) == 0.5f;
-    a.inv_denom = 1.0f / a.denom;
+    a.cdiv = const_div(a.denom);
     a.io = io;
     a.act = act;
     return dispatch_act(act, [&]<int A>() -> dnb_status {

@@ -59,8 +59,8 @@ struct TArgs {
     int R, SU, slot_floats, vec;
     int pf_from;     // first group whose share is prefetched into L2 (earlier ones fit the ring)
     int bulk_out;    // outputs leave by bulk copies from the slot (vec units, no x_norm)
-    float denom, inv_denom;
-    int denom_pow2;
+    float denom;
+    ConstDiv cdiv;  // division by denom, per element
     BnIO io;
     int act;
     unsigned long long *rec;  // this GPU's records [G][Ps][2 segments][4 words]
@@ -722,11 +722,7 @@ struct Stage {
                         for (int k = lane; k < n4; k += 32) {
                             const float4 d = d4[k], xv = x4[k];
                             const float4 yy = HASY ? y4[k] : xv;
-                            const float4 r =
-                                make_float4(bn_dx_p(bn_grad1<A, HASY>(d.x, xv.x, yy.x, p, a.act), xv.x, p, a),
-                                            bn_dx_p(bn_grad1<A, HASY>(d.y, xv.y, yy.y, p, a.act), xv.y, p, a),
-                                            bn_dx_p(bn_grad1<A, HASY>(d.z, xv.z, yy.z, p, a.act), xv.z, p, a),
-                                            bn_dx_p(bn_grad1<A, HASY>(d.w, xv.w, yy.w, p, a.act), xv.w, p, a));
+                            const float4 r = bn_dx4_p(bn_grad4<A, HASY>(d, xv, yy, p, a.act), xv, p, a);
                             if (a.bulk_out)
                                 d4[k] = r;  // over delta, element by element
                             else
@@ -1016,9 +1012,7 @@ dnb_status run_stage(int64_t batch, int64_t filters, int64_t spatial, int act, c
             count *= cv->world;  // normalize_delta divides by the element count of the whole batch
         }
         a.denom = (float)count;
-        int e2 = 0;
-        a.denom_pow2 = frexpf(a.denom, &e2) == 0.5f;
-        a.inv_denom = 1.0f / a.denom;
+        a.cdiv = const_div(a.denom);
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3((unsigned)P);
         cfg.blockDim = dim3(kTThreads);

@@ -196,6 +196,40 @@ def test_fused_backward(cuda, oracle, shape, act, with_y, bn_path):
     assert_close(vd_h, svd * fac, "variance_delta", scale=svdn * np.abs(fac))
 
 
+@pytest.mark.parametrize("shape", [(8, 16, 64), (16, 40, 196), (32, 64, 784), (4, 17, 53)])
+@pytest.mark.parametrize("act", [gpu.LEAKY, gpu.LINEAR])
+def test_fused_backward_edge_numerators(cuda, oracle, shape, act, bn_path):
+    """normalize_delta divides vd * 2 * (x - mean) by the element count (blas.zig:200); the
+    kernels replace the division by a verified two-operation form for numerators in its
+    range and divide the rest. Channels here make numerators of +0 and -0 (a constant
+    channel, elements equal to their channel's exact mean), tiny ones (delta ~ 1e-30) and
+    large ones (delta ~ 1e20): dx must still equal the reference's IEEE division bit for bit."""
+    B, C, S = shape
+    x, gamma, beta, delta, _, _ = make_inputs(shape, seed=11)
+    xv = x.reshape(B, C, S)
+    dv = delta.reshape(B, C, S)
+    xv[:, 0, :] = 1.5                                              # constant: x - mean = 0
+    xv[:, 1, :] = np.resize(np.float32([1.0, 1.5, 1.5, 2.0]), (B, S))  # mean 1.5: zeros where x = 1.5
+    dv[:, 2, :] = 0.0                                              # vd = 0
+    dv[:, 3, :] *= np.float32(1e-30)                               # tiny numerators
+    dv[:, 4 % C, :] *= np.float32(1e20)                            # large numerators
+    y = torch.empty(x.size, dtype=torch.float32, device="cuda")
+    mean = torch.zeros(C, device="cuda")
+    var = torch.zeros(C, device="cuda")
+    gpu.bnActForwardTrain(dev(x), y, None, B, C, S, dev(gamma), dev(beta), mean, var, torch.zeros(C, device="cuda"),
+                          torch.zeros(C, device="cuda"), act)
+    m, v, y_h = host(mean), host(var), host(y)
+    assert m[0] == np.float32(1.5)  # the constant channel's numerators are all zero
+    md = torch.zeros(C, device="cuda")
+    vd = torch.zeros(C, device="cuda")
+    bu, su = torch.zeros(C, device="cuda"), torch.zeros(C, device="cuda")
+    dxt = torch.empty_like(y)
+    gpu.bnActBackward(dev(x), None, dev(delta), dxt, B, C, S, dev(gamma), dev(beta), mean, var, bu, su, md, vd, act)
+    md_h, vd_h = host(md), host(vd)
+    _, _, dx_w = oracle_backward_given_stats(oracle, x, y_h, delta, shape, gamma, m, v, md_h, vd_h, act)
+    assert_bitexact(host(dxt), dx_w, "dx")
+
+
 def backward_sum_scales(oracle, x, y, delta, gamma, m, v, shape, act):
     """Per-channel 2-norms of the terms behind bias_updates, scale_updates, mean_delta and
     variance_delta (the scale of the reduction bar, parity.py)."""
