@@ -447,6 +447,7 @@ bool flat_cut_disabled() {
 constexpr int kSThreads = 512;              // threads of a sweep CTA
 constexpr int kSMinBlocks = 2;              // CTAs per SM the register budget is set for
 constexpr int kSWarps = kSThreads / 32 - 2;  // streaming warps; then the publisher and the merger
+constexpr unsigned kWaitSliceNs = 2000;      // longest suspension of one mbarrier try_wait
 
 template <bool BWD, int A, bool HASY>
 struct SweepKernel {
@@ -467,14 +468,14 @@ struct SweepKernel {
         float4 *ctab;    // [G][2 segments] channel inputs: (gamma, beta) or (mean, var, gamma, beta)
         double2 *lrec;   // [G][2 segments] this rank's merged records: (mean, M2) or (sum g, sum g(x-m))
         double *lcnt;    // [G][2 segments] elements behind the forward's records
-        int *done;       // [G] streaming warps that have left their partials of group g
-        int *ready;      // [G] 1 once the parameters of group g are in ptab
+        uint64_t *dbar;  // [G] mbarrier: every streaming warp has left its partials of group g
+        uint64_t *rbar;  // [G] mbarrier: the parameters of group g are in ptab
         int *stop;       // set by the merger warp when a wait gave up
     };
     __host__ __device__ static size_t smem_bytes(int cap_units, int groups) {
         return (((size_t)groups * cap_units * sizeof(uint32_t) + 15) & ~(size_t)15) +
                (size_t)groups * (2 * kSWarps * sizeof(float4) + 2 * sizeof(double2) + 2 * sizeof(double) +
-                                 16 * sizeof(float) + 4 * sizeof(float4) + 2 * sizeof(int)) +
+                                 16 * sizeof(float) + 4 * sizeof(float4) + 2 * sizeof(uint64_t)) +
                16;
     }
     __device__ static Smem carve(const PArgs &a, unsigned char *raw) {
@@ -495,25 +496,23 @@ struct SweepKernel {
         o += (size_t)G * 2 * sizeof(float4);
         s.ptab = reinterpret_cast<float *>(raw + o);
         o += (size_t)G * 16 * sizeof(float);
-        s.done = reinterpret_cast<int *>(raw + o);
-        o += (size_t)G * sizeof(int);
-        s.ready = reinterpret_cast<int *>(raw + o);
-        o += (size_t)G * sizeof(int);
+        s.dbar = reinterpret_cast<uint64_t *>(raw + o);  // 16-byte aligned: every block above is
+        o += (size_t)G * sizeof(uint64_t);
+        s.rbar = reinterpret_cast<uint64_t *>(raw + o);
+        o += (size_t)G * sizeof(uint64_t);
         s.stop = reinterpret_cast<int *>(raw + o);
         return s;
     }
 
-    // Bounded spin of a whole warp until *flag >= want; false if the merger warp stopped
-    // the CTA or the wait gave up (the latter sets the device error word).
-    __device__ static bool wait_smem(const PArgs &a, const Smem &s, const int *flag, int want) {
-        const volatile int *f = flag;
+    // Bounded wait of a whole warp for the (only) phase of a per-group mbarrier; false if
+    // the merger warp stopped the CTA or the wait gave up (the latter sets the device error
+    // word). The waiting warp is suspended in try_wait (up to kWaitSliceNs at a time) rather
+    // than spinning, so it takes no issue slots from the streaming warps.
+    __device__ static bool wait_bar(const PArgs &a, const Smem &s, uint64_t *bar) {
+        if (mbar_try_wait_ns(bar, 0u, 0u)) return true;
         const volatile int *stop = s.stop;
-        if (*f >= want) {
-            __threadfence_block();
-            return true;
-        }
         const unsigned long long deadline = global_ns() + a.wait_ns;
-        while (*f < want) {
+        while (!mbar_try_wait_ns(bar, 0u, kWaitSliceNs)) {
             if (*stop) return false;
             if (global_ns() > deadline) {
                 if ((threadIdx.x & 31) == 0) {
@@ -522,9 +521,7 @@ struct SweepKernel {
                 }
                 return false;
             }
-            __nanosleep(32);
         }
-        __threadfence_block();
         return true;
     }
 
@@ -708,7 +705,7 @@ struct SweepKernel {
             s.wrec[(2 * b + 0) * kSWarps + warp] = rec[0];
             s.wrec[(2 * b + 1) * kSWarps + warp] = rec[1];
             __threadfence_block();
-            atomicAdd(&s.done[b], 1);
+            mbar_arrive(&s.dbar[b]);  // releases the partials above
         }
         __syncwarp();
     }
@@ -996,7 +993,7 @@ __device__ void sweep_publisher(const PArgs &a, const typename SweepKernel<BWD, 
     using K = SweepKernel<BWD, A, HASY>;
     // groups in order, as soon as every streaming warp's partials are in
     for (int g = 0; g < a.G; ++g) {
-        if (!K::wait_smem(a, s, &s.done[g], kSWarps)) return;
+        if (!K::wait_bar(a, s, &s.dbar[g])) return;
         K::publish(a, s, g, rid, g, tag);
     }
 }
@@ -1015,11 +1012,8 @@ __device__ void sweep_merger(const PArgs &a, const typename SweepKernel<BWD, A, 
             if (lane == 0) *reinterpret_cast<volatile int *>(s.stop) = 1;
             return;
         }
-        K::finalize(a, s, g, rid);
-        if (lane == 0) {
-            __threadfence_block();
-            *reinterpret_cast<volatile int *>(&s.ready[g]) = 1;
-        }
+        K::finalize(a, s, g, rid);  // ends with __syncwarp: the lanes' ptab writes are in
+        if (lane == 0) mbar_arrive(&s.rbar[g]);
         __syncwarp();
         K::write_channels(a, s, g, rid);
     }
@@ -1032,7 +1026,7 @@ __device__ void sweep_streamer(const PArgs &a, const typename SweepKernel<BWD, A
     for (int h = 0; h < a.depth && h < a.G; ++h) K::template stats<FLAT>(a, s, h, rid, h);
     for (int g = 0; g < a.G; ++g) {
         if (g + a.depth < a.G) K::template stats<FLAT>(a, s, g + a.depth, rid, g + a.depth);
-        if (!K::wait_smem(a, s, &s.ready[g], 1)) return;  // group g's parameters
+        if (!K::wait_bar(a, s, &s.rbar[g])) return;  // group g's parameters
         K::template apply<FLAT>(a, s, g, rid, g);
     }
 }
@@ -1051,8 +1045,8 @@ __global__ void __launch_bounds__(kSThreads, kSMinBlocks) k_bn_sweep(PArgs a) {
         s_exited = 0;
     }
     if (threadIdx.x < a.G) {
-        s.done[threadIdx.x] = 0;
-        s.ready[threadIdx.x] = 0;
+        mbar_init(&s.dbar[threadIdx.x], kSWarps);
+        mbar_init(&s.rbar[threadIdx.x], 1);
     }
     for (int g = 0; g < a.G; ++g) K::tabulate(a, s, g, rid, g);
     // the backward's statistics pass needs the forward's parameters at once; the forward's

@@ -345,6 +345,19 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, unsigned by
 __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
+// try_wait with a suspend-time hint: the thread may sleep up to `ns` nanoseconds in the
+// instruction until the phase completes (no polling loop of its own in the meantime)
+__device__ __forceinline__ bool mbar_try_wait_ns(uint64_t *bar, unsigned parity, unsigned ns) {
+    unsigned ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity), "r"(ns)
+        : "memory");
+    return ok;
+}
 __device__ __forceinline__ bool mbar_test(uint64_t *bar, unsigned parity) {
     unsigned ok;
     asm volatile(
