@@ -26,13 +26,8 @@
 // statistics the outputs are bit-identical to it.
 #include <math.h>
 
-#include <string.h>
-
 #include <algorithm>
 #include <atomic>
-#include <mutex>
-#include <utility>
-#include <vector>
 
 #include "dnb_bn.cuh"
 
@@ -256,7 +251,7 @@ struct OpBwdApply {
     const float *x, *y, *d;
     float *dx;
     const BwdParam *tab;
-    float denom;
+    ConstDiv cdiv;  // division by the element count (normalize_delta)
     int act;
     bool vec;
     using P = BwdParam;
@@ -269,14 +264,24 @@ struct OpBwdApply {
         if (HASY) v.y = ld4(y + 4 * i);
         return v;
     }
-    __device__ float f(float dv, float xv, float yv, const P &p) const {
-        return bn_dx1(bn_grad1<A, HASY>(dv, xv, yv, p, act), xv, p, denom);
+    // dx as bn_dx1: (g*gamma)*inv2 + vd*2*(x-m)/denom + md/denom, the division by cdiv
+    __device__ static float num(float xv, const P &p) { return p.vd * 2.0f * (xv - p.m); }
+    __device__ static float dx1(float gv, const P &p, float q) { return (gv * p.g) * p.inv2 + q + p.mdd; }
+    __device__ float grad(float dv, float xv, float yv, const P &p) const {
+        return bn_grad1<A, HASY>(dv, xv, yv, p, act);
     }
     __device__ void store(int64_t i, V v, P p0, P p1, P p2, P p3) const {
-        st4(dx + 4 * i, make_float4(f(v.d.x, v.x.x, v.y.x, p0), f(v.d.y, v.x.y, v.y.y, p1),
-                                    f(v.d.z, v.x.z, v.y.z, p2), f(v.d.w, v.x.w, v.y.w, p3)));
+        const float4 q =
+            div4_const(make_float4(num(v.x.x, p0), num(v.x.y, p1), num(v.x.z, p2), num(v.x.w, p3)), cdiv);
+        st4(dx + 4 * i, make_float4(dx1(grad(v.d.x, v.x.x, v.y.x, p0), p0, q.x),
+                                    dx1(grad(v.d.y, v.x.y, v.y.y, p1), p1, q.y),
+                                    dx1(grad(v.d.z, v.x.z, v.y.z, p2), p2, q.z),
+                                    dx1(grad(v.d.w, v.x.w, v.y.w, p3), p3, q.w)));
     }
-    __device__ void scalar(int64_t i, P p) const { dx[i] = f(d[i], x[i], HASY ? y[i] : 0.0f, p); }
+    __device__ void scalar(int64_t i, P p) const {
+        const float xv = x[i];
+        dx[i] = dx1(grad(d[i], xv, HASY ? y[i] : 0.0f, p), p, div_const(num(xv, p), cdiv));
+    }
 };
 
 // Scratch layout of the generic path inside the workspace.
@@ -354,12 +359,13 @@ dnb_status generic_bwd_apply(const GGeom &g, const float *x, const float *y, con
         g.filters, denom, sums, mean, var, scales, biases, bias_upd, scale_upd, mean_delta, var_delta, tab);
     DNB_TRY(after_launch(s, "bn backward finalize"));
     const bool al = aligned16(x) && aligned16(delta) && aligned16(dx) && (!y || aligned16(y));
+    const ConstDiv cd = const_div(denom);
     return dispatch_act(act, [&]<int A>() {
         if (y)
             return chan::launch_chan(g.batch, g.filters, g.spatial,
-                                     OpBwdApply<A, true>{x, y, delta, dx, tab, denom, act, al}, s, "bn backward apply");
+                                     OpBwdApply<A, true>{x, y, delta, dx, tab, cd, act, al}, s, "bn backward apply");
         return chan::launch_chan(g.batch, g.filters, g.spatial,
-                                 OpBwdApply<A, false>{x, y, delta, dx, tab, denom, act, al}, s, "bn backward apply");
+                                 OpBwdApply<A, false>{x, y, delta, dx, tab, cd, act, al}, s, "bn backward apply");
     });
 }
 
@@ -1291,63 +1297,6 @@ dnb_status run_sweep(int64_t batch, int64_t filters, int64_t spatial, int act, c
 }
 
 }  // namespace
-
-// Verifies q = fma(a, zh, a * zl) against IEEE division a / d for every a in [1, 2) on the
-// host (float division and fmaf are correctly rounded there, as fma is on the device). The
-// verdict depends only on the significand of d: scaling d by 2^k scales zh and zl by 2^-k.
-// About 2^23 divisions, tens of milliseconds, once per significand and process.
-ConstDiv const_div(float d) {
-    ConstDiv k;
-    k.d = d;
-    k.lo = 0x7f800000u;  // no v takes the two-operation form until the check passes
-    if (!(d >= 1.0f) || !(d <= 0x1p40f)) return k;  // counts; zh and zl stay normal
-    k.zh = 1.0f / d;
-    k.zl = (float)(1.0 / (double)d - (double)k.zh);
-    int e2 = 0;
-    if (frexpf(d, &e2) == 0.5f) {  // 1/d is exact
-        k.pow2 = 1;
-        k.zl = 0.0f;
-        return k;
-    }
-    uint32_t dbits;
-    memcpy(&dbits, &d, 4);
-    const uint32_t key = dbits & 0x007fffffu;
-    static std::mutex mu;
-    static std::vector<std::pair<uint32_t, bool>> verdicts;
-    int known = -1;
-    {
-        std::lock_guard<std::mutex> lock(mu);
-        for (const auto &v : verdicts)
-            if (v.first == key) known = v.second ? 1 : 0;
-    }
-    if (known < 0) {
-        // the check runs on the divisor with the same significand in [1, 2)
-        int e = 0;
-        const float d1 = ldexpf(frexpf(d, &e), 1);
-        const float zh1 = 1.0f / d1;
-        const float zl1 = (float)(1.0 / (double)d1 - (double)zh1);
-        bool ok = true;
-        for (uint32_t m = 0; m < (1u << 23) && ok; ++m) {
-            const uint32_t bits = 0x3f800000u | m;
-            float a;
-            memcpy(&a, &bits, 4);
-            volatile float t = a * zl1;  // one rounding, as on the device (no contraction)
-            const float q = fmaf(a, zh1, t);
-            ok = q == a / d1;
-        }
-        std::lock_guard<std::mutex> lock(mu);
-        verdicts.emplace_back(key, ok);
-        known = ok ? 1 : 0;
-    }
-    if (!known) return k;
-    // |v| from which every intermediate is normal: |v * zl| >= 2^-126 and |v / d| >= 2^-126
-    // (factors of 2 for margin); below it, and for zero, v / d is divided
-    float lo = ldexpf(d, -124);
-    if (k.zl != 0.0f) lo = fmaxf(lo, ldexpf(1.0f, -125) / fabsf(k.zl));
-    if (lo < 0x1p127f) memcpy(&k.lo, &lo, 4);
-    return k;
-}
-
 }  // namespace dnb
 
 using namespace dnb;

@@ -7,6 +7,7 @@
 // its compulsory bytes per element. Arithmetic is bit-identical to the reference CPU
 // ops: --fmad=false keeps a*b+c as two roundings, and __fmaf_rn appears exactly where
 // blas.axpy fuses.
+#include "dnb_cdiv.cuh"
 #include "dnb_chan.cuh"
 
 namespace dnb {
@@ -277,13 +278,14 @@ struct OpNormalize {
 struct NDParam {
     float inv, vd, md_over, m;
 };
-__device__ __forceinline__ float norm_delta1(float d, float x, const NDParam &p, float denom) {
-    return d * p.inv + p.vd * 2.0f * (x - p.m) / denom + p.md_over;
-}
+// the division by the element count is done by the launch's ConstDiv (dnb_cdiv.cuh)
+__device__ __forceinline__ float norm_delta_num(float x, const NDParam &p) { return p.vd * 2.0f * (x - p.m); }
+__device__ __forceinline__ float norm_delta1(float d, const NDParam &p, float q) { return d * p.inv + q + p.md_over; }
 struct OpNormalizeDelta {
     const float *x, *mean, *var, *md, *vd;
     float *d;
     float denom;
+    ConstDiv cdiv;
     bool vec;
     using P = NDParam;
     struct V { float4 d, x; };
@@ -297,10 +299,13 @@ struct OpNormalizeDelta {
     }
     __device__ V load(int64_t i) const { return {ld4(d + 4 * i), ld4(x + 4 * i)}; }
     __device__ void store(int64_t i, V v, P p0, P p1, P p2, P p3) const {
-        st4(d + 4 * i, make_float4(norm_delta1(v.d.x, v.x.x, p0, denom), norm_delta1(v.d.y, v.x.y, p1, denom),
-                                   norm_delta1(v.d.z, v.x.z, p2, denom), norm_delta1(v.d.w, v.x.w, p3, denom)));
+        const float4 q = div4_const(make_float4(norm_delta_num(v.x.x, p0), norm_delta_num(v.x.y, p1),
+                                                norm_delta_num(v.x.z, p2), norm_delta_num(v.x.w, p3)),
+                                    cdiv);
+        st4(d + 4 * i, make_float4(norm_delta1(v.d.x, p0, q.x), norm_delta1(v.d.y, p1, q.y),
+                                   norm_delta1(v.d.z, p2, q.z), norm_delta1(v.d.w, p3, q.w)));
     }
-    __device__ void scalar(int64_t i, P p) const { d[i] = norm_delta1(d[i], x[i], p, denom); }
+    __device__ void scalar(int64_t i, P p) const { d[i] = norm_delta1(d[i], p, div_const(norm_delta_num(x[i], p), cdiv)); }
 };
 
 // Inference BN + activation (batchnorm.zig:147-152 + convolutional.zig:269):
@@ -434,7 +439,8 @@ dnb_status dnb_normalize_delta(const float *x, const float *mean, const float *v
     if (batch * filters * spatial > 0 && (!x || !mean || !variance || !mean_delta || !variance_delta || !delta))
         return fail(DNB_ERR_INVALID, "normalize_delta: null pointer");
     const float denom = (float)(spatial * batch);  // blas.zig:191
-    OpNormalizeDelta op{x, mean, variance, mean_delta, variance_delta, delta, denom, aligned16(x) && aligned16(delta)};
+    OpNormalizeDelta op{x,     mean,  variance,        mean_delta, variance_delta,
+                        delta, denom, const_div(denom), aligned16(x) && aligned16(delta)};
     return launch_chan(batch, filters, spatial, op, as_stream(stream), "normalize_delta");
 }
 
