@@ -398,6 +398,8 @@ struct PArgs {
     int cpu, cpu_s;           // chunks per unit of the output pass / of the statistics pass
     FastDiv f_cpu, f_cpu_s;
     FastDiv f_u4;             // U / 4: float4s of a unit (the flat chunk cut)
+    int nread, nwrite;        // streaming warps taking statistics / writing outputs (both kSWarps
+                              // unless the roles are split: nread + nwrite = kSWarps)
     unsigned *sync;           // [0] launch epoch, [1] CTAs that have finished this launch
     unsigned *err, *abort_flag;
     unsigned long long wait_ns;
@@ -454,6 +456,7 @@ constexpr int kSThreads = 512;              // threads of a sweep CTA
 constexpr int kSMinBlocks = 2;              // CTAs per SM the register budget is set for
 constexpr int kSWarps = kSThreads / 32 - 2;  // streaming warps; then the publisher and the merger
 constexpr unsigned kWaitSliceNs = 2000;      // longest suspension of one mbarrier try_wait
+constexpr int kSplitReaders = 7;             // statistics warps when the roles are split
 
 template <bool BWD, int A, bool HASY>
 struct SweepKernel {
@@ -476,12 +479,13 @@ struct SweepKernel {
         double *lcnt;    // [G][2 segments] elements behind the forward's records
         uint64_t *dbar;  // [G] mbarrier: every streaming warp has left its partials of group g
         uint64_t *rbar;  // [G] mbarrier: the parameters of group g are in ptab
+        uint64_t *abar;  // [G] mbarrier (split roles): every output warp is done with group g
         int *stop;       // set by the merger warp when a wait gave up
     };
     __host__ __device__ static size_t smem_bytes(int cap_units, int groups) {
         return (((size_t)groups * cap_units * sizeof(uint32_t) + 15) & ~(size_t)15) +
                (size_t)groups * (2 * kSWarps * sizeof(float4) + 2 * sizeof(double2) + 2 * sizeof(double) +
-                                 16 * sizeof(float) + 4 * sizeof(float4) + 2 * sizeof(uint64_t)) +
+                                 16 * sizeof(float) + 4 * sizeof(float4) + 3 * sizeof(uint64_t)) +
                16;
     }
     __device__ static Smem carve(const PArgs &a, unsigned char *raw) {
@@ -505,6 +509,8 @@ struct SweepKernel {
         s.dbar = reinterpret_cast<uint64_t *>(raw + o);  // 16-byte aligned: every block above is
         o += (size_t)G * sizeof(uint64_t);
         s.rbar = reinterpret_cast<uint64_t *>(raw + o);
+        o += (size_t)G * sizeof(uint64_t);
+        s.abar = reinterpret_cast<uint64_t *>(raw + o);
         o += (size_t)G * sizeof(uint64_t);
         s.stop = reinterpret_cast<int *>(raw + o);
         return s;
@@ -647,7 +653,7 @@ struct SweepKernel {
         if constexpr (!BWD) {
             Moments mo;
             float4 first = make_float4(0.0f, 0.0f, 0.0f, 0.0f);  // segment 0 once the warp moved on
-            for (uint32_t c = warp; c < n_chunks; c += kSWarps) {
+            for (uint32_t c = warp; c < n_chunks; c += (uint32_t)a.nread) {
                 const int cs = lanes_at<CHUNK_S, FLAT>(a, w, ut, a.f_cpu_s, c, lane, off, ok);
                 if (cs != seg) {  // warp-uniform
                     first = mo.warp_summary();
@@ -667,7 +673,7 @@ struct SweepKernel {
             rec[1] = seg ? last : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         } else {
             float s1 = 0.0f, s2 = 0.0f, f1 = 0.0f, f2 = 0.0f;  // f: segment 0 once the warp moved on
-            for (uint32_t c = warp; c < n_chunks; c += kSWarps) {
+            for (uint32_t c = warp; c < n_chunks; c += (uint32_t)a.nread) {
                 const int cs = lanes_at<CHUNK_S, FLAT>(a, w, ut, a.f_cpu_s, c, lane, off, ok);
                 if (cs != seg) {
                     f1 = s1;
@@ -722,7 +728,7 @@ struct SweepKernel {
         const Share sh = share_of(a, g, rid, a.f_ps);
         const int lane = threadIdx.x & 31;
         for (int j = 0; j < sh.nseg; ++j) {
-            float4 q = lane < kSWarps ? s.wrec[(2 * b + j) * kSWarps + lane] : make_float4(0, 0, 0, 0);
+            float4 q = lane < a.nread ? s.wrec[(2 * b + j) * kSWarps + lane] : make_float4(0, 0, 0, 0);
             if constexpr (!BWD) {
 #pragma unroll
                 for (int o = 16; o > 0; o >>= 1) {
@@ -935,7 +941,7 @@ struct SweepKernel {
     __device__ static void apply(const PArgs &a, const Smem &s, int g, int rid, int b) {
         const Share sh = share_of(a, g, rid, a.f_ps);
         if (sh.nseg == 0) return;
-        const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+        const int warp = (threadIdx.x >> 5) - (a.nwrite < kSWarps ? a.nread : 0), lane = threadIdx.x & 31;
         const Walk w = walk_of<CHUNK, FLAT>(a, sh, a.cpu);
         const uint32_t n_chunks = w.n_chunks;
         const uint32_t *ut = s.utab + b * a.cap_units;
@@ -944,7 +950,7 @@ struct SweepKernel {
         uint32_t offs[UNROLL];
         bool ok[UNROLL];
         if constexpr (!BWD) {
-            for (uint32_t c = warp; c < n_chunks; c += kSWarps) {
+            for (uint32_t c = warp; c < n_chunks; c += (uint32_t)a.nwrite) {
                 const int cs = lanes_at<CHUNK, FLAT>(a, w, ut, a.f_cpu, c, lane, offs, ok);
                 const float4 p = *reinterpret_cast<const float4 *>(ptab + 8 * cs);
                 float4 v[UNROLL];
@@ -969,7 +975,7 @@ struct SweepKernel {
                     }
             }
         } else {
-            for (uint32_t c = warp; c < n_chunks; c += kSWarps) {
+            for (uint32_t c = warp; c < n_chunks; c += (uint32_t)a.nwrite) {
                 const int cs = lanes_at<CHUNK, FLAT>(a, w, ut, a.f_cpu, c, lane, offs, ok);
                 const BwdParam p = *reinterpret_cast<const BwdParam *>(ptab + 8 * cs);
                 float4 d[UNROLL], xv[UNROLL], yv[UNROLL];
@@ -1029,6 +1035,26 @@ __device__ void sweep_streamer(const PArgs &a, const typename SweepKernel<BWD, A
     using K = SweepKernel<BWD, A, HASY>;
     // statistics of groups 0 .. lag-1, then per group g the statistics of group g + lag
     // followed by the outputs of group g
+    if (a.nwrite < kSWarps) {
+        // split roles: warps below nread read the statistics of every group, the others write
+        // the outputs; a reader starts group h once the writers are done with group
+        // h - lag - 1, so at most lag + 1 groups wait in L2
+        const int warp = threadIdx.x >> 5;
+        if (warp < a.nread) {
+            for (int h = 0; h < a.G; ++h) {
+                if (h > a.depth && !K::wait_bar(a, s, &s.abar[h - a.depth - 1])) return;
+                K::template stats<FLAT>(a, s, h, rid, h);
+            }
+        } else {
+            for (int g = 0; g < a.G; ++g) {
+                if (!K::wait_bar(a, s, &s.rbar[g])) return;
+                K::template apply<FLAT>(a, s, g, rid, g);
+                __syncwarp();
+                if ((threadIdx.x & 31) == 0) mbar_arrive(&s.abar[g]);
+            }
+        }
+        return;
+    }
     for (int h = 0; h < a.depth && h < a.G; ++h) K::template stats<FLAT>(a, s, h, rid, h);
     for (int g = 0; g < a.G; ++g) {
         if (g + a.depth < a.G) K::template stats<FLAT>(a, s, g + a.depth, rid, g + a.depth);
@@ -1051,7 +1077,8 @@ __global__ void __launch_bounds__(kSThreads, kSMinBlocks) k_bn_sweep(PArgs a) {
         s_exited = 0;
     }
     if (threadIdx.x < a.G) {
-        mbar_init(&s.dbar[threadIdx.x], kSWarps);
+        mbar_init(&s.dbar[threadIdx.x], (unsigned)a.nread);
+        mbar_init(&s.abar[threadIdx.x], (unsigned)a.nwrite);
         mbar_init(&s.rbar[threadIdx.x], 1);
     }
     for (int g = 0; g < a.G; ++g) K::tabulate(a, s, g, rid, g);
@@ -1250,6 +1277,17 @@ dnb_status run_sweep(int64_t batch, int64_t filters, int64_t spatial, int act, c
         // work behind) 65.1 us against 55.5 us
         [[maybe_unused]] const bool flat = BWD && (pl.U / 4) % chunk != 0 && !flat_cut_disabled();
         a.f_u4 = FastDiv((uint32_t)(pl.U / 4));
+        // Split roles: kSplitReaders streaming warps take the statistics and the others write
+        // the outputs, concurrently, so HBM reads go on while outputs are written from L2. It
+        // pays in the backward over many groups: measured on the B200, [128,256,28,28] (7
+        // groups) 90.8 against 95.5 us, [256,256,28,28] (13) 175.0 against 181.1 us, and
+        // within 0.6 % either way at [128,196,32,32] and [128,64,56,56] (7); with 4 groups it
+        // lost ([128,128,32,32] 55.7 against 52.5 us), and every forward measured slower.
+        // DNB_BN_SPLIT=r forces r readers (0: every streaming warp does both passes).
+        const int split_auto = BWD && pl.G >= 6 ? kSplitReaders : 0;
+        a.nread = env_int("DNB_BN_SPLIT", split_auto, 0, kSWarps - 1);
+        a.nwrite = a.nread ? kSWarps - a.nread : kSWarps;
+        if (!a.nread) a.nread = kSWarps;
         a.act = act;
         a.rec = ws->recs;
         a.rec_words = ws->rec_words;

@@ -48,6 +48,9 @@ FULL_SHAPES = [(128, 128, 1024), (128, 256, 784), (64, 128, 1024)]
 BN_PATHS = {
     "default": {},
     "sweep": {"DNB_BN_SMALL": "0", "DNB_BN_CLUSTER": "0", "DNB_BN_STAGE": "0"},
+    # the sweep with its streaming warps split into statistics readers and output writers (the
+    # default only for backwards over many channel groups)
+    "sweep-split": {"DNB_BN_SMALL": "0", "DNB_BN_CLUSTER": "0", "DNB_BN_STAGE": "0", "DNB_BN_SPLIT": "7"},
     "cluster": {"DNB_BN_SMALL": "0", "DNB_BN_SWEEP": "0"},
     "stage": {"DNB_BN_SMALL": "0", "DNB_BN_CLUSTER": "0", "DNB_BN_SWEEP": "0"},
     "generic": {"DNB_BN_PERSISTENT": "0"},

@@ -23,10 +23,11 @@ pytestmark = pytest.mark.gpu
 
 PATHS = {
     "sweep": {"DNB_BN_SMALL": "0", "DNB_BN_CLUSTER": "0", "DNB_BN_STAGE": "0"},
+    "sweep-split": {"DNB_BN_SMALL": "0", "DNB_BN_CLUSTER": "0", "DNB_BN_STAGE": "0", "DNB_BN_SPLIT": "7"},
     "cluster": {"DNB_BN_SMALL": "0", "DNB_BN_SWEEP": "0"},
     "stage": {"DNB_BN_SMALL": "0", "DNB_BN_CLUSTER": "0", "DNB_BN_SWEEP": "0"},
 }
-SHAPES = [(64, 64, 3136), (16, 40, 196), (32, 256, 196)]
+SHAPES = [(64, 64, 3136), (16, 40, 196), (32, 256, 196), (128, 256, 784)]
 REPEATS = 60
 
 
