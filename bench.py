@@ -193,7 +193,15 @@ class ClockSampler:
                 stdout=self.out, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
-        time.sleep(0.3)  # the first sample lands before the timed region starts
+            return
+        # the timed regions start once the tool prints (its start-up takes longer on boxes with
+        # more GPUs); give up after 5 s and fall back to one reading after the regions
+        deadline = time.time() + 5.0
+        while time.time() < deadline and self.proc.poll() is None:
+            self.out.flush()
+            if os.fstat(self.out.fileno()).st_size > 0:
+                break
+            time.sleep(0.02)
 
     def stop(self):
         rows = []
