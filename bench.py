@@ -901,7 +901,7 @@ def run_reference(a):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    threads = os.cpu_count() or 1
+    threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
     B, C, H, W = a.shape
     gpu_kernels = ref_gpu_kernels(a)
     t, E, NW = cpu_step_sample(a, threads, a.steps, min(a.warmup, 3))
@@ -920,9 +920,12 @@ def run_reference(a):
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic (seeded splitmix64 generator)",
-        "config": {"workload": workload_desc(a, 1), "baseline_config": a.config, "batch_per_gpu": B, "channels": C,
-                   "hw": [H, W], "sgd_weights_per_gpu": NW,
-                   "parallelism": "host cores (reference CPU ops, OpenMP over channels / elements)"},
+        # the same workload string as this library's line at the same --gpus; the host computes one
+        # rank's shard (the reference has no multi-GPU path), whose GB/s is the step's rate
+        "config": {"workload": workload_desc(a, a.gpus), "baseline_config": a.config, "batch_per_gpu": B,
+                   "channels": C, "hw": [H, W], "sgd_weights_per_gpu": NW,
+                   "parallelism": "host cores (reference CPU ops, OpenMP over channels / elements), one "
+                                  "rank's shard"},
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
                          "sample": f"{a.steps} full steps (after {min(a.warmup, 3)} warm-up) of the reference op "
                                    f"sequence batchnorm.zig:74-123 + activations.zig"
