@@ -177,14 +177,14 @@ struct OpSgd {
     float a_decay, a_lr, mom;
     bool vec;
     struct V { float4 w, u; };
-    __device__ V load(int64_t i) const { return {ld4_stream(w + 4 * i), ld4_stream(wu + 4 * i)}; }
+    __device__ V load(int64_t i) const { return {ld4(w + 4 * i), ld4(wu + 4 * i)}; }
     __device__ void store(int64_t i, V v) const {
         sgd1(v.w.x, v.u.x, a_decay, a_lr, mom);
         sgd1(v.w.y, v.u.y, a_decay, a_lr, mom);
         sgd1(v.w.z, v.u.z, a_decay, a_lr, mom);
         sgd1(v.w.w, v.u.w, a_decay, a_lr, mom);
-        st4_stream(w + 4 * i, v.w);
-        st4_stream(wu + 4 * i, v.u);
+        st4(w + 4 * i, v.w);
+        st4(wu + 4 * i, v.u);
     }
     __device__ void scalar(int64_t i) const {
         float a = w[i], b = wu[i];
