@@ -1039,6 +1039,22 @@ def run_ops(a):
         timed("bn_act_backward", f"{label} leaky", 12 * E, make_bnt,
               lambda t, b_=b_, c_=c_, s_=s_: gpu.bnActBackward(t[0], None, t[2], t[3], b_, c_, s_, t[4], t[5], t[6],
                                                                t[7], t[10], t[11], t[12], t[13], LEAKY_))
+        if s_ % 4 == 0:
+            # the forward from a producer's statistics: one (count, mean, M2) per 128-pixel tile
+            # and channel, as a GEMM epilogue would leave them; x read once, y written once
+            npc = -(-(b_ * s_) // 128)
+
+            def make_fs(i, E=E, c_=c_, npc=npc, n_=b_ * s_):
+                pc = torch.zeros((npc, c_, 3), dtype=torch.float64, device="cuda")
+                pc[:, :, 0] = 128.0
+                pc[-1, :, 0] = float(n_ - 128 * (npc - 1))
+                pc[:, :, 2] = pc[:, :, 0]
+                return (torch.randn(E, **f32), torch.empty(E, **f32), pc, torch.rand(c_, **f32) + 0.5,
+                        torch.randn(c_, **f32) * 0.1, *(torch.zeros(c_, **f32) for _ in range(4)))
+
+            timed("bn_act_forward_from_stats", f"{label} leaky, {npc} tiles of statistics", 8 * E + 24 * npc * c_,
+                  make_fs, lambda t, b_=b_, c_=c_, s_=s_, npc=npc: gpu.bnActForwardFromStats(
+                      t[0], t[1], None, b_, c_, s_, t[2], npc, t[3], t[4], t[5], t[6], t[7], t[8], LEAKY_))
     # the BLAS-1 basics on 64 Mi floats
     timed("fill", "64 Mi floats", 4 * n, lambda i: (torch.empty(n, **f32),), lambda t: gpu.fill(t[0], n, 0.5))
     timed("copy", "64 Mi floats", 8 * n, lambda i: (torch.randn(n, **f32), torch.empty(n, **f32)),

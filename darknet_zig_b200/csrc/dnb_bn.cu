@@ -166,6 +166,55 @@ __global__ void k_fwd_finalize(int64_t filters, int ranks, double count_per_rank
     tab[c] = make_float4(f.m, f.inv, scales[c], biases[c]);
 }
 
+// Forward finalize from a producer's statistics: npieces blocks [piece][filters] of (count, mean,
+// M2). A block takes 32 channels and 32 slices of the pieces: lane l of warp w reads channel
+// c0 + l of pieces w, w + 32, ... (a warp's loads are 32 consecutive channels of one piece) and
+// keeps, in fp64 about a shift K (the channel's first piece's mean), n, sum n d and sum (M2 + n d^2)
+// with d = mean_p - K; the 32 slices of a channel are then added in slice order through shared
+// memory, and M2 = sum (M2 + n d^2) - (sum n d)^2 / n. One pass over the pieces, no division per
+// piece, the same result on every launch.
+constexpr int kPieceCh = 32, kPieceSlices = 32;
+__global__ void __launch_bounds__(kPieceCh * kPieceSlices)
+    k_fwd_finalize_pieces(int64_t filters, int64_t npieces, const double *pieces, const float *scales,
+                          const float *biases, float *mean, float *var, float *rmean, float *rvar, float4 *tab) {
+    __shared__ double3 part[kPieceSlices][kPieceCh];
+    const int lane = threadIdx.x & 31, slice = threadIdx.x >> 5;
+    const int64_t c = (int64_t)blockIdx.x * kPieceCh + lane;
+    double sn = 0.0, snd = 0.0, sq = 0.0;
+    // the shift: the first piece's mean when that piece is not empty (its mean is then data)
+    const double K = c < filters && pieces[c * 3] > 0.0 ? pieces[c * 3 + 1] : 0.0;
+    if (c < filters) {
+#pragma unroll 4
+        for (int64_t p = slice; p < npieces; p += kPieceSlices) {
+            const double *q = pieces + (p * filters + c) * 3;
+            const double nb = q[0], d = q[1] - K, m2 = q[2];
+            if (nb > 0.0) {
+                sn += nb;
+                snd += nb * d;
+                sq += m2 + nb * d * d;
+            }
+        }
+    }
+    part[slice][lane] = make_double3(sn, snd, sq);
+    __syncthreads();
+    if (slice != 0 || c >= filters) return;
+    double n = 0.0, s1 = 0.0, s2 = 0.0;
+    for (int w = 0; w < kPieceSlices; ++w) {
+        const double3 t = part[w][lane];
+        n += t.x;
+        s1 += t.y;
+        s2 += t.z;
+    }
+    double m2 = s2 - s1 * (s1 / n);
+    if (m2 < 0.0) m2 = 0.0;
+    const FwdClose f = fwd_close(K + s1 / n, m2, n);
+    mean[c] = f.m;
+    var[c] = f.var;
+    rmean[c] = rolling(rmean[c], f.m);
+    rvar[c] = rolling(rvar[c], f.var);
+    tab[c] = make_float4(f.m, f.inv, scales[c], biases[c]);
+}
+
 template <int A>
 struct OpFwdApply {
     const float *x;
@@ -1536,6 +1585,33 @@ dnb_status dnb_syncbn_act_backward(dnb_comm comm, const float *x, const float *y
     }
     if (!launched) return fail(DNB_ERR_UNSUPPORTED, "%s: shape not taken by the fused kernel", what);
     return DNB_OK;
+}
+
+dnb_status dnb_bn_act_forward_from_stats(const float *x, float *y, float *x_norm, int64_t batch, int64_t filters,
+                                         int64_t spatial, const double *pieces, int64_t npieces,
+                                         const float *scales, const float *biases, float *mean, float *variance,
+                                         float *rolling_mean, float *rolling_variance, int act,
+                                         dnb_stream stream) {
+    const char *what = "bn_act_forward_from_stats";
+    DNB_TRY(check_shape(batch, filters, spatial, what));
+    if (!valid_act(act)) return fail(DNB_ERR_INVALID, "%s: unknown activation %d", what, act);
+    if (npieces < 1) return fail(DNB_ERR_INVALID, "%s: npieces must be >= 1", what);
+    if (filters == 0) return DNB_OK;
+    if (!x || !y || !pieces || !scales || !biases || !mean || !variance || !rolling_mean || !rolling_variance)
+        return fail(DNB_ERR_INVALID, "%s: null pointer", what);
+    const cudaStream_t s = as_stream(stream);
+    const GGeom g = make_ggeom(batch, filters, spatial, aligned16(x));
+    Workspace *ws = nullptr;
+    DNB_TRY(workspace(s, GScratch::bytes(g), &ws));
+    const GScratch sc = GScratch::carve(ws->scratch, g);
+    float4 *tab = static_cast<float4 *>(sc.tab);
+    k_fwd_finalize_pieces<<<(unsigned)((filters + kPieceCh - 1) / kPieceCh), kPieceCh * kPieceSlices, 0, s>>>(
+        filters, npieces, pieces, scales, biases, mean, variance, rolling_mean, rolling_variance, tab);
+    DNB_TRY(after_launch(s, what));
+    const bool al = aligned16(x) && aligned16(y) && (!x_norm || aligned16(x_norm));
+    return dispatch_act(act, [&]<int A>() {
+        return chan::launch_chan(batch, filters, spatial, OpFwdApply<A>{x, y, x_norm, tab, act, al}, s, what);
+    });
 }
 
 dnb_status dnb_syncbn_forward_partials(const float *x, int64_t batch, int64_t filters, int64_t spatial,

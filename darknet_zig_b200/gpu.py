@@ -223,6 +223,16 @@ def bnActForwardInfer(x, y, batch, filters, spatial, scales, biases, rolling_mea
          _p(rolling_mean), _p(rolling_variance), int(act), _s())
 
 
+def bnActForwardFromStats(x, y, x_norm, batch, filters, spatial, pieces, npieces, scales, biases, mean,  # noqa: N802
+                          variance, rolling_mean, rolling_variance, act):
+    """Training forward from the producer's per-piece (count, mean, M2) statistics, fp64
+    [npieces][filters][3]; no counterpart in gpu.zig."""
+    call("bn_act_forward_from_stats", _p(x), _p(y), _p(x_norm), int(batch), int(filters), int(spatial),
+         _p(pieces, torch.float64),
+         int(npieces), _p(scales), _p(biases), _p(mean), _p(variance), _p(rolling_mean), _p(rolling_variance),
+         int(act), _s())
+
+
 def bnActBackward(x, y, delta, dx, batch, filters, spatial, scales, biases, mean_in, variance_in,  # noqa: N802
                   bias_updates, scale_updates, mean_delta_out, variance_delta_out, act):
     call("bn_act_backward", _p(x), _p(y), _p(delta), _p(dx), int(batch), int(filters), int(spatial), _p(scales),

@@ -223,6 +223,20 @@ dnb_status dnb_bn_act_forward_train(const float *x, float *y, float *x_norm, int
 dnb_status dnb_bn_act_forward_infer(const float *x, float *y, int64_t batch, int64_t filters, int64_t spatial,
                                     const float *scales, const float *biases, const float *rolling_mean,
                                     const float *rolling_variance, int act, dnb_stream stream);
+/* Training forward from statistics that the producer of x computed (a convolution's GEMM
+ * epilogue per output tile, say: convolutional.zig:239-270 runs the convolution and then
+ * batchnorm.zig:129-153 reads its output twice, once for the statistics): pieces holds
+ * npieces blocks laid out [piece][filters][3] = (count, mean, M2) of disjoint pieces of each
+ * channel, fp64, with each channel's counts adding up to batch*spatial (pieces with count 0
+ * are skipped). The pieces are merged in piece order (Chan's parallel variance), mean,
+ * variance and the rolling statistics are written as by dnb_bn_act_forward_train, and
+ * BN + activation are applied to x: one pass over x (8 bytes per element), no statistics
+ * pass. No reference counterpart. */
+dnb_status dnb_bn_act_forward_from_stats(const float *x, float *y, float *x_norm, int64_t batch, int64_t filters,
+                                         int64_t spatial, const double *pieces, int64_t npieces,
+                                         const float *scales, const float *biases, float *mean, float *variance,
+                                         float *rolling_mean, float *rolling_variance, int act,
+                                         dnb_stream stream);
 /* Backward through activation and batchnorm in one HBM pass: replaces gpu.gradientArray
  * (convolutional.zig:280) + batchnorm.backwardGpu (batchnorm.zig:155-169).
  *   x      the forward's input (l.x); delta = dL/dy (l.delta) on entry.

@@ -53,6 +53,8 @@ def test_error_strings(built_lib):
     ("shortcut", (1, 0, 4, 4, None, 4, 4, 4, C.c_float(1), C.c_float(1), None, None)),
     ("sgd_momentum", (16, None, None, C.c_float(0.1), C.c_float(0.9), C.c_float(5e-4), 128, None)),
     ("syncbn_forward_apply", (None, None, None, 2, 4, 4, None, 0, None, None, None, None, None, None, 7, None)),
+    ("bn_act_forward_from_stats", (None, None, None, 2, 4, 4, None, 0, None, None, None, None, None, None, 7, None)),
+    ("bn_act_forward_from_stats", (None, None, None, 2, 4, 4, None, 3, None, None, None, None, None, None, 99, None)),
 ])
 def test_bad_arguments_are_rejected_without_a_device(built_lib, name, args):
     lib = _lib.lib()
