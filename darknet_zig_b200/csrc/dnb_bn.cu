@@ -313,7 +313,7 @@ struct OpBwdApply {
         if (HASY) v.y = ld4(y + 4 * i);
         return v;
     }
-    // dx as bn_dx1: (g*gamma)*inv2 + vd*2*(x-m)/denom + md/denom, the division by cdiv
+    // dx = (g*gamma)*inv2 + vd*2*(x-m)/denom + md/denom (blas.zig:200), the division by cdiv
     __device__ static float num(float xv, const P &p) { return p.vd * 2.0f * (xv - p.m); }
     __device__ static float dx1(float gv, const P &p, float q) { return (gv * p.g) * p.inv2 + q + p.mdd; }
     __device__ float grad(float dv, float xv, float yv, const P &p) const {

@@ -127,10 +127,6 @@ __device__ __forceinline__ float4 bn_grad4(float4 d, float4 x, float4 y, const B
     return make_float4(bn_grad1<A, HASY>(d.x, x.x, y.x, p, act), bn_grad1<A, HASY>(d.y, x.y, y.y, p, act),
                        bn_grad1<A, HASY>(d.z, x.z, y.z, p, act), bn_grad1<A, HASY>(d.w, x.w, y.w, p, act));
 }
-// dx = (g*gamma)*inv2 + vd*2*(x-m)/denom + md/denom (blas.zig:200 on delta*scales)
-__device__ __forceinline__ float bn_dx1(float gval, float x, const BwdParam &p, float denom) {
-    return (gval * p.g) * p.inv2 + p.vd * 2.0f * (x - p.m) / denom + p.mdd;
-}
 
 
 // A record is 4 64-bit words, each (tag << 32 | a float's bits): naturally aligned 64-bit
@@ -204,7 +200,8 @@ template <class Args>
 __device__ __forceinline__ float div_denom(float v, const Args &a) {
     return div_const(v, a.cdiv);
 }
-// dx as bn_dx1, the division by the element count done by the launch's ConstDiv
+// dx = (g*gamma)*inv2 + vd*2*(x-m)/denom + md/denom (blas.zig:200 on delta*scales), the division
+// by the element count done by the launch's ConstDiv
 template <class Args>
 __device__ __forceinline__ float bn_dx_p(float gval, float x, const BwdParam &p, const Args &a) {
     return (gval * p.g) * p.inv2 + div_denom(p.vd * 2.0f * (x - p.m), a) + p.mdd;
